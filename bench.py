@@ -1,0 +1,464 @@
+#!/usr/bin/env python
+"""Decode-attention benchmark: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2]
+                    [--shard dp|tp] [--scaling weak|strong] [--impl b2d|reference]
+
+A step is one decode of the workload's whole batch (BASELINE config 2 by
+default: GQA paged, B=64, Hq=32, Hkv=8, D=128, bf16, lengths ~ U[1024, 8192],
+page 16, permuted pages).  For N > 1 the script runs under
+torch.distributed.run, one process per GPU over NCCL:
+
+* --scaling weak (default): every rank decodes its own full batch (seed +
+  rank); no collective inside the step.
+* --scaling strong --shard dp: the batch is split across ranks by a greedy
+  length balance; no collective inside the step.
+* --scaling strong --shard tp: KV heads are split across ranks and the
+  outputs are all-gathered over NCCL inside the step.
+
+Timing: W warm-up steps, then K steps between CUDA events on the launching
+stream, bracketed by barrier + synchronize, max over ranks.  The KV cache of
+one step (1.2 GB for config 2) is ~10x the 126 MB L2, so no flush is needed
+between steps.  `value` is achieved HBM TB/s over all ranks (algorithmic
+bytes / step time); `roofline` times the split-KV kernel alone.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import platform
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "roofline-analysis_b200"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "decode attention µs/step and achieved HBM TB/s (% of roofline) at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b2d", "reference"], default="b2d")
+    ap.add_argument("--workload", default="cfg2")
+    ap.add_argument("--shard", choices=["dp", "tp"], default="dp")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU work budget of the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch (smaller profiling cases)")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------
+# environment helpers
+# --------------------------------------------------------------------------
+
+def measured_hbm_peak():
+    try:
+        d = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(workload: str):
+    """Per-launch DRAM bytes of the split-KV kernel from the committed ncu
+    summary (profiles/traffic.json), or None."""
+    try:
+        d = json.loads((REPO / "profiles" / "traffic.json").read_text())
+        return d.get(workload)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self):
+        if self.nv is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        names = [n for n, bit in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+def dist_setup():
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def reduce_over_ranks(x: float, world: int, device, op) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=op)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------
+# CPU baseline: the reference's SDPA call on host cores
+# --------------------------------------------------------------------------
+
+def cpu_sample_inputs(w, x, n_seqs):
+    """The first n sequences of the workload as dense CPU tensors (gather not
+    timed) -> (q, dense_kv, algorithmic bytes, n)."""
+    from oracle.sdpa_cpu import gather_dense
+    from b200decode import workloads as W
+    n = max(1, min(n_seqs, x["q"].shape[0]))
+    sl = x["cache_seqlens"][:n].cpu()
+    bt = x["block_table"][:n].cpu()
+    page = x["k_cache"].shape[1]
+    used = torch.unique(torch.cat([bt[i, : (int(l) + page - 1) // page]
+                                   for i, l in enumerate(sl.tolist())]).long())
+    kc = torch.zeros(tuple(x["k_cache"].shape), dtype=x["k_cache"].dtype)
+    vc = torch.zeros_like(kc)
+    kc[used] = x["k_cache"][used.to(x["k_cache"].device)].cpu()
+    vc[used] = x["v_cache"][used.to(x["v_cache"].device)].cpu()
+    ks = None if x.get("k_scale") is None else x["k_scale"].cpu()
+    vs = None if x.get("v_scale") is None else x["v_scale"].cpu()
+    dense = gather_dense(kc, vc, sl, bt, ks, vs)
+    q = x["q"][:n].cpu()
+    return q, dense, W.gqa_algorithmic_bytes(w.scaled(batch=n), sl), n
+
+
+def time_cpu_sdpa(q, dense, scale, seconds):
+    """Median seconds per pass of the SDPA decode over the sample, repeating
+    passes for about `seconds` of CPU work (at least 3 passes)."""
+    from oracle.sdpa_cpu import sdpa_decode
+    torch.set_num_threads(os.cpu_count() or 1)
+    sdpa_decode(q, dense, scale)  # warm-up
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < 3 or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        sdpa_decode(q, dense, scale)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 200:
+            break
+    return statistics.median(times), len(times)
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor()
+
+
+# --------------------------------------------------------------------------
+# main
+# --------------------------------------------------------------------------
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_setup()
+    from b200decode import workloads as W
+
+    w0 = W.get(args.workload)
+    if args.batch:
+        w0 = w0.scaled(batch=args.batch)
+    if not isinstance(w0, W.GqaWorkload):
+        raise SystemExit("bench.py measures the GQA decode workloads (cfg1/cfg2/cfg3/cfg5)")
+
+    if args.impl == "reference":
+        return run_reference_arm(args, world, rank, w0)
+
+    import b200decode
+    from b200decode import _lib, shard
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    SUM, MAX = dist.ReduceOp.SUM, dist.ReduceOp.MAX
+
+    # ---- inputs ----
+    tp = args.scaling == "strong" and args.shard == "tp" and world > 1
+    if args.scaling == "weak" or world == 1:
+        w = w0.scaled(seed=w0.seed + rank) if world > 1 else w0
+        x = W.make_gqa_inputs(w, dev)
+        par = f"dp{world}-weak" if world > 1 else "single"
+    else:
+        xg = W.make_gqa_inputs(w0, dev)
+        if args.shard == "dp":
+            rows = shard.balance_sequences(xg["cache_seqlens"].tolist(), world)[rank]
+            x = shard.slice_gqa_inputs_by_batch(xg, rows)
+            w = w0.scaled(batch=len(rows))
+        else:
+            x = shard.slice_gqa_inputs_by_heads(xg, world, rank)
+            w = w0.scaled(num_kv_heads=w0.num_kv_heads // world,
+                          num_q_heads=w0.num_q_heads // world)
+        del xg
+        torch.cuda.empty_cache()
+        par = f"{args.shard}{world}"
+    sl = x["cache_seqlens"].cpu()
+    local_bytes = W.gqa_algorithmic_bytes(w, sl)
+
+    def dec(**kw):
+        return b200decode.decode(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"],
+                                 x["block_table"], x["softmax_scale"], k_scale=x["k_scale"],
+                                 v_scale=x["v_scale"], **kw)
+
+    def step():
+        out, lse = dec()
+        if tp:
+            out, lse = shard.gather_heads(out, lse)
+        return out, lse
+
+    # launches of our kernels per step: split-KV + combine per batch slice
+    n_ctas, chunk, hk_cta = b200decode.gqa_plan(x["q"], x["k_cache"], x["v_cache"],
+                                                x["cache_seqlens"], x["block_table"])
+    slices = max(1, math.ceil(w.batch * (w.num_kv_heads // hk_cta) / 2048))
+    launches_per_step = 2 * slices
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    b200decode.check_device_status()
+
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = reduce_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, dev, MAX)
+    total_bytes = reduce_over_ranks(local_bytes, world, dev, SUM)
+    total_flops = reduce_over_ranks(W.gqa_flops(w, sl), world, dev, SUM)
+    total_kv_ref = reduce_over_ranks(W.gqa_kv_bytes_reference(w, sl), world, dev, SUM)
+    total_tokens = reduce_over_ranks(int(sl.sum()), world, dev, SUM)
+    tbs = total_bytes / (ms * 1e-3) / 1e12
+
+    # ---- the split-KV kernel and the combine kernel alone ----
+    def timed(flag, n):
+        for _ in range(3):
+            dec(flags=flag)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(n):
+            dec(flags=flag)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) / n
+
+    kk = max(5, args.steps)
+    kern_ms = timed(_lib.B2D_FLAG_SKIP_COMBINE, kk)
+    combine_ms = timed(_lib.B2D_FLAG_COMBINE_ONLY, kk)
+    peak, peak_kind = measured_hbm_peak()
+    achieved_gbs = local_bytes / (kern_ms * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        qh = x["q"].cpu().pin_memory()
+        slh = x["cache_seqlens"].cpu().pin_memory()
+        bth = x["block_table"].cpu().pin_memory()
+        qd, sld, btd = (torch.empty_like(x["q"]), torch.empty_like(x["cache_seqlens"]),
+                        torch.empty_like(x["block_table"]))
+        hq_out = w0.num_q_heads if tp else w.num_q_heads
+        out_h = torch.empty((w.batch, hq_out, w.head_dim), dtype=x["q"].dtype).pin_memory()
+        lse_h = torch.empty((w.batch, hq_out), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            qd.copy_(qh, non_blocking=True)
+            sld.copy_(slh, non_blocking=True)
+            btd.copy_(bth, non_blocking=True)
+            out, lse = b200decode.decode(qd, x["k_cache"], x["v_cache"], sld, btd,
+                                         x["softmax_scale"], k_scale=x["k_scale"],
+                                         v_scale=x["v_scale"])
+            if tp:
+                out, lse = shard.gather_heads(out, lse)
+            out_h.copy_(out, non_blocking=True)
+            lse_h.copy_(lse, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = reduce_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, dev, MAX)
+        h2d = qh.numel() * qh.element_size() + slh.numel() * 4 + bth.numel() * 4
+        d2h = out_h.numel() * out_h.element_size() + lse_h.numel() * 4
+        e2e = {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+               "us_per_step": round(e2e_ms * 1e3, 2),
+               "h2d_bytes_per_step": int(reduce_over_ranks(h2d, world, dev, SUM)),
+               "d2h_bytes_per_step": int(reduce_over_ranks(d2h, world, dev, SUM))}
+
+    # ---- CPU baseline (rank 0, N = 1) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        q_s, dense, sbytes, n = cpu_sample_inputs(w, x, min(4, w.batch))
+        sec, reps = time_cpu_sdpa(q_s, dense, x["softmax_scale"], args.cpu_seconds)
+        cpu = {"value": round(sbytes / sec / 1e12, 6), "unit": "TB/s",
+               "cores": torch.get_num_threads(), "kind": "reference",
+               "sample": (f"torch.nn.functional.scaled_dot_product_attention on CPU (the call of "
+                          f"decodebench/torch_sdpa_benchmark.py:100-102, enable_gqa) over the "
+                          f"first {n} of {w.batch} sequences ({int(sl[:n].sum())} tokens), pages "
+                          f"gathered untimed; median of {reps} passes, {sec * 1e3:.1f} ms each"),
+               "cpu_model": cpu_model(), "os_cpu_count": os.cpu_count()}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(tbs, 4), "unit": "TB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
+            "us_per_step": round(ms * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak" if (args.scaling == "weak" or world == 1) else "strong",
+            "vs_baseline": None,
+            "pct_hbm_roofline": round(100 * tbs / (peak * world / 1e3), 2),
+            "dtype": "fp8-e4m3 KV, bf16 q, fp32 accumulate" if w0.kv_dtype == "fp8"
+                     else f"{w0.kv_dtype} in, fp32 accumulate",
+            "data": ("synthetic: seeded N(0,1) q/K/V, lengths ~ U[%d,%d], random page permutation"
+                     % (w0.seqlen_lo, w0.seqlen_hi)),
+            "config": {"workload": w0.name, "batch": w0.batch, "num_q_heads": w0.num_q_heads,
+                       "num_kv_heads": w0.num_kv_heads, "head_dim": w0.head_dim,
+                       "page_size": w0.page_size, "kv_dtype": w0.kv_dtype, "parallelism": par,
+                       "tokens_per_step": int(total_tokens),
+                       "algorithmic_bytes_per_step": int(total_bytes),
+                       "approx_kv_bytes_read": int(total_kv_ref),
+                       "flops_per_step": int(total_flops),
+                       "l2": "each step reads >1 GB of KV (> 126 MB L2); no flush between steps",
+                       "num_ctas": n_ctas, "chunk_tokens": chunk, "kv_heads_per_cta": hk_cta},
+            "roofline": {"bound": "hbm", "kernel": "b2d::gqa_decode_kernel",
+                         "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved_gbs / peak, 4), "peak_source": peak_kind,
+                         "traffic": committed_traffic(w0.name),
+                         "kernel_us": round(kern_ms * 1e3, 2),
+                         "combine_us": round(combine_ms * 1e3, 2),
+                         "bytes_per_launch": int(local_bytes)},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference_arm(args, world, rank, w0):
+    """The reference's CPU decode path (torch SDPA on host cores), timed on
+    rank 0 only, each step a bounded sample of the same workload."""
+    if rank != 0:
+        return
+    from b200decode import workloads as W
+    from oracle.sdpa_cpu import sdpa_decode
+    torch.set_num_threads(os.cpu_count() or 1)
+    seqlens = W.draw_seqlens(w0.batch, w0.seqlen_lo, w0.seqlen_hi, w0.seed)
+    budget = max(0.2, 120.0 / (args.steps + max(3, args.warmup)))
+    n = 1
+    while True:   # grow the sample while one pass stays under half the budget
+        ws = w0.scaled(batch=n)
+        xs = W.make_gqa_inputs(ws, "cpu", seqlens=seqlens[:n])
+        q, dense, nbytes, _ = cpu_sample_inputs(ws, xs, n)
+        t0 = time.perf_counter()
+        sdpa_decode(q, dense, ws.softmax_scale)
+        dt = time.perf_counter() - t0
+        if dt * 4 > budget or n >= w0.batch:
+            break
+        n = min(w0.batch, n * 2)
+    for _ in range(max(3, args.warmup)):
+        sdpa_decode(q, dense, ws.softmax_scale)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        sdpa_decode(q, dense, ws.softmax_scale)
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    tbs = nbytes / sec / 1e12
+    sample = (f"torch SDPA (decodebench/torch_sdpa_benchmark.py:100-102) on CPU over {n} of "
+              f"{w0.batch} sequences ({int(seqlens[:n].sum())} tokens) per step, pages gathered "
+              f"untimed")
+    line = {"impl": "reference", "metric": METRIC, "value": round(tbs, 6), "unit": "TB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": w0.kv_dtype, "data": "synthetic",
+            "config": {"workload": w0.name, "batch": w0.batch, "parallelism": "host cores",
+                       "sample_sequences": n},
+            "cpu_baseline": {"value": round(tbs, 6), "unit": "TB/s",
+                             "cores": torch.get_num_threads(), "kind": "reference",
+                             "sample": sample, "cpu_model": cpu_model()},
+            "e2e": {"value": round(tbs, 6), "unit": "TB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,182 @@
+/*
+ * b2d_decode.h — C ABI of the B200 (sm_100a) decode-attention library
+ * (libb2d.so).  Plain pointers, sizes and enums only: no C++ or torch types.
+ *
+ * What this boundary replaces.  The reference (meinie0826/Roofline-Analysis,
+ * decodebench/) times one library call per backend inside a
+ * `<X>Kernel(DecodeShape).run()` adapter.  These entry points are the single
+ * call such an adapter makes:
+ *
+ *   b2d_decode_gqa  replaces
+ *     decodebench/flashattn_kvcache_kernel.py:150-169
+ *         flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens,
+ *                                 block_table, causal=True) -> (out, lse)
+ *     decodebench/flashinfer_kernel.py:115-116
+ *         BatchDecodeWithPagedKVCacheWrapper.run(q, (k_cache, v_cache))
+ *     decodebench/trtllm_decode_kernel.py:102-113
+ *         trtllm_batch_decode_with_kv_cache(...)  (HND cache: pass strides)
+ *     decodebench/vllm_paged_kernel.py:203-222
+ *         ops.paged_attention_v2(...)  (split-KV partials + reduce)
+ *   b2d_decode_mla  replaces
+ *     decodebench/trtllm_mla_kernel.py:115-132
+ *         trtllm_batch_decode_with_kv_cache_mla(query, kv_cache, ...)
+ *   the split merge inside both follows
+ *     cute_attention/cluster_decode/cluster_decode_reduce.py:67-91
+ *         merge_split_kv_decode_partials (M = max m; L = sum l e^(m-M); ...)
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless stated otherwise.  Strides are
+ *     in ELEMENTS; the innermost (head_dim) dimension must be contiguous.
+ *   - All calls are enqueue-only on `stream` (a cudaStream_t, NULL = legacy
+ *     default stream); none synchronises or allocates.  The caller owns all
+ *     memory including the workspace (size from the *_workspace_bytes call).
+ *   - Return value 0 = success, negative = b2d_status code; a human-readable
+ *     message comes from b2d_error_string().  Nothing aborts the process.
+ *   - lse is the natural-log log-sum-exp of the scaled scores, fp32.
+ */
+#ifndef B2D_DECODE_H_
+#define B2D_DECODE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (0 = ok). */
+enum b2d_status {
+  B2D_OK = 0,
+  B2D_ERR_INVALID_ARG = -1,      /* null pointer, bad size, bad stride      */
+  B2D_ERR_UNSUPPORTED = -2,      /* head_dim / dtype / group not built      */
+  B2D_ERR_ALIGNMENT = -3,        /* base or stride not 16-byte aligned      */
+  B2D_ERR_WORKSPACE = -4,        /* workspace missing or too small          */
+  B2D_ERR_CUDA = -5,             /* a CUDA runtime/driver call failed       */
+  B2D_ERR_DEVICE_TIMEOUT = -6,   /* a kernel gave up waiting (status word)  */
+  B2D_ERR_DEVICE_BOUNDS = -7,    /* a kernel saw a page id out of range     */
+  B2D_ERR_TOO_LARGE = -8         /* a size beyond the documented maximum    */
+};
+
+/* Launch flags, for measuring the two kernels of a decode separately.
+ * SKIP_COMBINE enqueues only the split-KV kernel (rows split across CTAs are
+ * then left as partials in the workspace); COMBINE_ONLY enqueues only the
+ * merge, over the partials the previous identical call left. */
+enum b2d_flags {
+  B2D_FLAG_SKIP_COMBINE = 1,
+  B2D_FLAG_COMBINE_ONLY = 2
+};
+
+/* Element types. */
+enum b2d_dtype {
+  B2D_BF16 = 0,
+  B2D_FP16 = 1,
+  B2D_FP8_E4M3 = 2,
+  B2D_FP32 = 3
+};
+
+/*
+ * Paged GQA/MHA/MQA decode: one query token per sequence.
+ *   q        [batch, num_q_heads, head_dim]               (bf16 | fp16)
+ *   k_cache  [num_pages, page_size, num_kv_heads, head_dim] (NHD, default) or
+ *            any other order of (page, token, head) given by the strides, e.g.
+ *            TRT-LLM HND [num_pages, 2, num_kv_heads, page_size, head_dim].
+ *            Element type = q's type, or FP8_E4M3 with k_scale/v_scale.
+ *   cache_seqlens [batch] int32, block_table [batch, max_pages_per_seq] int32
+ *   k_scale, v_scale: fp32 [num_kv_heads] dequantisation scales (FP8 only;
+ *            value = e4m3 * scale).  NULL means 1.0.
+ *   out      [batch, num_q_heads, head_dim] in q's type;  lse [batch,
+ *            num_q_heads] fp32 (may be NULL).
+ * Query head h reads KV head h / (num_q_heads / num_kv_heads).
+ * A sequence of length 0 yields out = 0 and lse = -inf.
+ */
+typedef struct b2d_gqa_args {
+  const void* q;
+  int64_t q_stride_b, q_stride_h;
+  const void* k_cache;
+  const void* v_cache;
+  int64_t k_stride_page, k_stride_tok, k_stride_head;
+  int64_t v_stride_page, v_stride_tok, v_stride_head;
+  int64_t num_pages;
+  const int32_t* cache_seqlens;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  const float* k_scale;
+  const float* v_scale;
+  void* out;
+  int64_t out_stride_b, out_stride_h;
+  float* lse;
+  int64_t lse_stride_b;
+  int32_t batch, num_q_heads, num_kv_heads, head_dim, page_size;
+  int32_t max_pages_per_seq;
+  int32_t q_dtype, kv_dtype;
+  float softmax_scale;
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t num_ctas;        /* 0 = one resident wave on this device          */
+  int32_t flags;           /* B2D_FLAG_* (0 = normal decode)                */
+  int32_t reserved[2];
+} b2d_gqa_args;
+
+/* Workspace bytes that b2d_decode_gqa needs for these arguments (pointers
+ * may be NULL here; only sizes, dtypes and num_ctas are read). */
+int b2d_gqa_workspace_bytes(const b2d_gqa_args* args, size_t* bytes);
+
+/* Enqueue the decode (split-KV kernel, then the LSE combine when a
+ * sequence was split across CTAs). */
+int b2d_decode_gqa(const b2d_gqa_args* args, void* stream);
+
+/*
+ * Absorbed-MLA decode (DeepSeek-V3 shape): every query head attends to one
+ * shared latent KV head.  Scores use all head_dim_qk (= 576: 512 latent + 64
+ * rope) columns; V is the first head_dim_v (= 512) columns of the same row.
+ *   q        [batch, num_heads, head_dim_qk] bf16
+ *   kv_cache [num_pages, page_size, head_dim_qk] bf16 (row stride given)
+ *   out      [batch, num_heads, head_dim_v] bf16; lse [batch, num_heads] fp32
+ */
+typedef struct b2d_mla_args {
+  const void* q;
+  int64_t q_stride_b, q_stride_h;
+  const void* kv_cache;
+  int64_t kv_stride_page, kv_stride_tok;
+  int64_t num_pages;
+  const int32_t* cache_seqlens;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  void* out;
+  int64_t out_stride_b, out_stride_h;
+  float* lse;
+  int64_t lse_stride_b;
+  int32_t batch, num_heads, head_dim_qk, head_dim_v, page_size;
+  int32_t max_pages_per_seq;
+  int32_t dtype;
+  float softmax_scale;
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t num_ctas;        /* 0 = auto                                      */
+  int32_t flags;           /* B2D_FLAG_* (0 = normal decode)                */
+  int32_t reserved[2];
+} b2d_mla_args;
+
+int b2d_mla_workspace_bytes(const b2d_mla_args* args, size_t* bytes);
+int b2d_decode_mla(const b2d_mla_args* args, void* stream);
+
+/*
+ * Reads (and clears, when clear != 0) the device status word that kernels
+ * set when an in-kernel wait ran out of time or a page id was out of range.
+ * Synchronises `stream`.  Returns 0 or the matching negative b2d_status.
+ */
+int b2d_check_device_status(void* workspace, int clear, void* stream);
+
+/* Split plan the GQA kernel would use: number of CTAs and KV tokens per
+ * pipeline chunk (host-only, no GPU access beyond a cached SM count). */
+int b2d_gqa_plan(const b2d_gqa_args* args, int32_t* num_ctas,
+                 int32_t* chunk_tokens, int32_t* kv_heads_per_cta);
+
+const char* b2d_error_string(int status);
+const char* b2d_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2D_DECODE_H_ */

@@ -1,0 +1,24 @@
+"""b200decode — B200-native (sm_100a) paged decode attention.
+
+Host layer over libb2d.so (hand-written CUDA kernels behind a C ABI,
+include/b2d_decode.h).  Public API:
+
+    decode(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale)
+        -> (out, lse)
+    decode_mla(q, kv_cache, cache_seqlens, block_table, softmax_scale)
+        -> (out, lse)
+
+There is no CPU or library fallback: calling either without the compiled
+library or without a CUDA device raises.
+"""
+from .api import (  # noqa: F401
+    B2DError,
+    DecodeWorkspace,
+    check_device_status,
+    decode,
+    decode_mla,
+    gqa_plan,
+    library_path,
+)
+
+__version__ = "0.1.0"

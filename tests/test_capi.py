@@ -1,0 +1,96 @@
+"""The C-ABI library: loads, exports every declared symbol, validates
+arguments on the host (no GPU needed for any call made here)."""
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from b200decode import _lib
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _declared():
+    names = set()
+    for h in (REPO / "include").glob("*.h"):
+        names |= set(re.findall(r"\b(b2d_[a-z0-9_]+)\s*\(", h.read_text()))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = _declared()
+    assert declared, "no declarations found"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r" T (b2d_\w+)", out))
+    assert declared <= exported, f"missing: {declared - exported}"
+    for name in declared:
+        assert hasattr(lib, name)
+    assert set(_lib.EXPORTED) <= declared
+
+
+def test_error_strings_and_version():
+    lib = _lib.load()
+    assert lib.b2d_error_string(0) == b"ok"
+    for code in range(-1, -9, -1):
+        assert lib.b2d_error_string(code) != b"unknown b2d status"
+    assert b"sm_100a" in lib.b2d_version()
+
+
+def _args(**kw):
+    a = _lib.GqaArgs()
+    a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim = 64, 32, 8, 128
+    a.page_size, a.max_pages_per_seq = 16, 512
+    a.q_dtype, a.kv_dtype = _lib.B2D_BF16, _lib.B2D_BF16
+    a.num_ctas = 296
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_workspace_query_and_plan_on_host():
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    assert lib.b2d_gqa_workspace_bytes(C.byref(_args()), C.byref(n)) == 0
+    # status + row_start + (rows + ctas) * heads * (D + 1) floats
+    assert n.value >= (64 + 296) * 32 * 129 * 4
+    nc, t, hk = C.c_int32(), C.c_int32(), C.c_int32()
+    assert lib.b2d_gqa_plan(C.byref(_args()), C.byref(nc), C.byref(t), C.byref(hk)) == 0
+    assert (nc.value, hk.value) == (296, 8) and 16 % t.value == 0
+    # GQA group 8 -> two warps per KV head, four KV heads per CTA
+    assert lib.b2d_gqa_plan(C.byref(_args(num_q_heads=64)), C.byref(nc), C.byref(t), C.byref(hk)) == 0
+    assert hk.value == 4
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(head_dim=96), -2),                 # unsupported head_dim
+    (dict(num_q_heads=30), -1),              # not a multiple of num_kv_heads
+    (dict(q_dtype=_lib.B2D_FP8_E4M3), -2),   # q must be 16-bit
+    (dict(kv_dtype=_lib.B2D_FP16), -2),      # cache must match q or be fp8
+    (dict(num_q_heads=8 * 64), -2),          # group 64 not built
+    (dict(page_size=0), -1),
+])
+def test_host_validation_rejects(kw, code):
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    assert lib.b2d_gqa_workspace_bytes(C.byref(_args(**kw)), C.byref(n)) == code
+
+
+def test_decode_rejects_null_pointers_before_touching_a_gpu():
+    lib = _lib.load()
+    assert lib.b2d_decode_gqa(C.byref(_args()), None) == -1
+    assert lib.b2d_decode_gqa(None, None) == -1
+    assert lib.b2d_decode_gqa(C.byref(_args(batch=0)), None) == 0  # no-op
+
+
+def test_python_layer_refuses_cpu_tensors():
+    import torch
+    import b200decode
+    q = torch.zeros(1, 4, 64, dtype=torch.bfloat16)
+    kc = torch.zeros(1, 16, 1, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        b200decode.decode(q, kc, kc, torch.ones(1, dtype=torch.int32),
+                          torch.zeros(1, 1, dtype=torch.int32))

@@ -1,0 +1,194 @@
+"""GPU parity of the split-KV GQA decode kernel against the CPU oracle,
+called through the C ABI (b200decode.decode -> libb2d.so)."""
+import numpy as np
+import pytest
+import torch
+
+import b200decode
+from b200decode import workloads as W
+from helpers import assert_parity, oracle_gqa, to_oracle
+from oracle import decode_ref as R
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(x, **kw):
+    out, lse = b200decode.decode(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"],
+                                 x["block_table"], x["softmax_scale"], k_scale=x["k_scale"],
+                                 v_scale=x["v_scale"], **kw)
+    torch.cuda.synchronize()
+    b200decode.check_device_status()
+    return out, lse
+
+
+def _inputs(cuda, w, lens=None):
+    sl = None if lens is None else torch.tensor(lens, dtype=torch.int64)
+    return W.make_gqa_inputs(w, cuda, seqlens=sl)
+
+
+SMALL = W.GqaWorkload("small", 5, 8, 2, 128, 16, "bf16", 1, 300, seed=3)
+
+
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (8, 4), (8, 2), (16, 2), (32, 4), (32, 1), (6, 2), (3, 1)])
+def test_group_sizes(cuda, hq, hkv):
+    x = _inputs(cuda, SMALL.scaled(num_q_heads=hq, num_kv_heads=hkv))
+    out, lse = _run(x)
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+@pytest.mark.parametrize("d", [64, 128, 256])
+@pytest.mark.parametrize("dt", ["bf16", "fp16", "fp8"])
+def test_head_dims_and_dtypes(cuda, d, dt):
+    qdt = "fp16" if dt == "fp16" else "bf16"
+    w = SMALL.scaled(head_dim=d, kv_dtype=dt, q_dtype=qdt,
+                     kv_scale_range=(0.01, 0.1) if dt == "fp8" else None)
+    x = _inputs(cuda, w)
+    out, lse = _run(x)
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+@pytest.mark.parametrize("page", [1, 4, 8, 16, 32, 64, 128, 48])
+def test_page_sizes(cuda, page):
+    w = SMALL.scaled(page_size=page)
+    x = _inputs(cuda, w, lens=[1, page - 1 if page > 1 else 2, page, page + 1, 3 * page + 5])
+    out, lse = _run(x)
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+def test_empty_and_tiny_sequences(cuda):
+    x = _inputs(cuda, SMALL, lens=[0, 1, 0, 2, 17])
+    out, lse = _run(x)
+    assert_parity(out, lse, *oracle_gqa(x))
+    assert torch.all(out[0] == 0) and torch.all(torch.isneginf(lse[0]))
+
+
+def test_all_empty_batch(cuda):
+    x = _inputs(cuda, SMALL, lens=[0, 0, 0])
+    out, lse = _run(x)
+    assert torch.all(out == 0) and torch.all(torch.isneginf(lse))
+
+
+@pytest.mark.parametrize("num_ctas", [1, 2, 3, 7, 64, 296, 1000])
+def test_split_counts_agree(cuda, num_ctas):
+    """Every CTA count partitions the same work differently (whole rows,
+    split rows, rows over many CTAs, more CTAs than chunks); all must match."""
+    x = _inputs(cuda, SMALL.scaled(batch=4, seqlen_lo=1, seqlen_hi=2000))
+    out, lse = _run(x, num_ctas=num_ctas)
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+def test_hnd_layout_and_strided_views(cuda):
+    """TRT-LLM-style HND cache [pages, 2, Hkv, P, D] passed as K/V views."""
+    x = _inputs(cuda, SMALL.scaled(page_size=64))
+    kc, vc = x["k_cache"], x["v_cache"]
+    both = torch.stack([kc.permute(0, 2, 1, 3), vc.permute(0, 2, 1, 3)], dim=1).contiguous()
+    out, lse = b200decode.decode(x["q"], both[:, 0], both[:, 1], x["cache_seqlens"],
+                                 x["block_table"], x["softmax_scale"], kv_layout="HND")
+    torch.cuda.synchronize()
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+def test_q_with_token_axis_and_preallocated_outputs(cuda):
+    x = _inputs(cuda, SMALL)
+    q4 = x["q"][:, None]
+    out = torch.full_like(q4, float("nan"))
+    lse = torch.full((q4.shape[0], q4.shape[2]), float("nan"), device=cuda)
+    o2, l2 = b200decode.decode(q4, x["k_cache"], x["v_cache"], x["cache_seqlens"],
+                               x["block_table"], x["softmax_scale"], out=out, lse=lse)
+    torch.cuda.synchronize()
+    assert o2 is out and l2 is lse
+    assert_parity(out[:, 0], lse, *oracle_gqa(x))
+
+
+def test_nan_in_page_tail_is_ignored(cuda):
+    """Slots past a sequence's length (same page) hold garbage; they must not
+    leak into the result."""
+    x = _inputs(cuda, SMALL, lens=[5, 19])
+    bt = x["block_table"].cpu()
+    for b, l in enumerate([5, 19]):
+        last = bt[b, (l - 1) // 16].item()
+        x["k_cache"][last, l % 16:] = float("nan")
+        x["v_cache"][last, l % 16:] = float("inf")
+    out, lse = _run(x)
+    assert torch.isfinite(out.float()).all()
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+def test_batch_larger_than_one_launch(cuda):
+    """More than 2048 rows: the host slices the batch into launches."""
+    w = SMALL.scaled(batch=2100, num_q_heads=4, num_kv_heads=1, head_dim=64, seqlen_lo=1, seqlen_hi=40)
+    x = _inputs(cuda, w)
+    out, lse = _run(x)
+    rows = np.r_[0:5, 2040:2060, 2095:2100]
+    ref_out, ref_lse = oracle_gqa(x, rows=rows)
+    assert_parity(out, lse, ref_out, ref_lse, rows=rows)
+
+
+def test_deterministic(cuda):
+    x = _inputs(cuda, SMALL.scaled(batch=8, seqlen_hi=3000))
+    o1, l1 = _run(x)
+    o2, l2 = _run(x)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+
+
+def test_out_of_range_page_id_is_reported(cuda):
+    """The kernel clamps a bad page id to page 0 (no out-of-bounds access)
+    and records it in the status word."""
+    x = _inputs(cuda, SMALL, lens=[20, 20])
+    x["block_table"][1, 0] = x["k_cache"].shape[0] + 5
+    b200decode.decode(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"], x["block_table"])
+    with pytest.raises(b200decode.B2DError, match="out of range"):
+        b200decode.check_device_status()
+    b200decode.check_device_status()  # cleared
+
+
+def test_errors_surface_as_exceptions(cuda):
+    x = _inputs(cuda, SMALL)
+    with pytest.raises(ValueError):
+        b200decode.decode(x["q"].float(), x["k_cache"], x["v_cache"], x["cache_seqlens"], x["block_table"])
+    with pytest.raises(ValueError):
+        b200decode.decode(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"].long(), x["block_table"])
+
+
+# ---------------- BASELINE configurations at full size ----------------
+
+def test_cfg1_mha_dense(cuda):
+    x = _inputs(cuda, W.CFG1_MHA_CPU)
+    out, lse = _run(x)
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+def test_cfg2_gqa_paged_full(cuda):
+    x = _inputs(cuda, W.CFG2_GQA_PAGED)
+    out, lse = _run(x)
+    rows = np.array([0, 1, 17, 40, 63])
+    ref_out, ref_lse = oracle_gqa(x, rows=rows)
+    assert_parity(out, lse, ref_out, ref_lse, rows=rows)
+
+
+def test_cfg5_fp8_full(cuda):
+    x = _inputs(cuda, W.CFG5_FP8)
+    out, lse = _run(x)
+    rows = np.array([0, 100, 255])
+    ref_out, ref_lse = oracle_gqa(x, rows=rows)
+    assert_parity(out, lse, ref_out, ref_lse, rows=rows)
+
+
+def test_cfg3_long_context_full(cuda):
+    """B=4 x 131072 tokens: oracle on KV head 0 of sequences 0 and 3, plus
+    invariance of the result under a very different split count."""
+    w = W.CFG3_LONG_SPLITKV
+    x = _inputs(cuda, w)
+    out, lse = _run(x)
+    g = w.num_q_heads // w.num_kv_heads
+    for b in (0, 3):
+        L = int(x["cache_seqlens"][b])
+        pages = x["block_table"][b, : (L + w.page_size - 1) // w.page_size].long()
+        k = to_oracle(x["k_cache"][pages][:, :, 0].reshape(-1, w.head_dim)[:L])[None]
+        v = to_oracle(x["v_cache"][pages][:, :, 0].reshape(-1, w.head_dim)[:L])[None]
+        q = to_oracle(x["q"][b, :g])
+        ro, rl = R.dense_decode(q, k, v, w.softmax_scale)
+        assert_parity(out[b, :g], lse[b, :g], ro, rl)
+    out2, lse2 = _run(x, num_ctas=37)
+    assert (out2.float() - out.float()).abs().max().item() < 1e-2
+    assert (lse2 - lse).abs().max().item() < 1e-4

@@ -1,0 +1,96 @@
+"""Host logic: seeded workloads, block tables, byte accounting, sharding
+(including a world-size-2 gloo all-gather on CPU)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from b200decode import shard
+from b200decode import workloads as W
+
+
+def test_block_table_is_a_permutation_of_the_pool():
+    sl = W.draw_seqlens(64, 1024, 8192, 0)
+    bt, n = W.make_block_table(sl, 16, True, 0)
+    used = torch.cat([bt[b, : (int(l) + 15) // 16] for b, l in enumerate(sl.tolist())])
+    assert n == sum((int(l) + 15) // 16 for l in sl.tolist())
+    assert sorted(used.tolist()) == list(range(n))
+    assert used.tolist() != list(range(n))  # permuted
+
+
+def test_seeded_and_bounded():
+    a = W.draw_seqlens(64, 1024, 8192, 0)
+    assert torch.equal(a, W.draw_seqlens(64, 1024, 8192, 0))
+    assert int(a.min()) >= 1024 and int(a.max()) <= 8192
+
+
+def test_algorithmic_bytes_cfg2_near_survey_figure():
+    sl = W.draw_seqlens(64, 1024, 8192, 0)
+    b = W.gqa_algorithmic_bytes(W.CFG2_GQA_PAGED, sl)
+    kv = W.gqa_kv_bytes_reference(W.CFG2_GQA_PAGED, sl)
+    assert kv == int(sl.sum()) * 8 * 128 * 2 * 2
+    assert 0 < b - kv < 2_000_000
+    assert W.gqa_algorithmic_bytes(W.CFG3_LONG_SPLITKV, torch.full((4,), 131072)) > 2_147_483_648
+
+
+def test_balance_sequences_covers_each_once_and_balances():
+    sl = W.draw_seqlens(256, 2048, 8192, 0).tolist()
+    parts = shard.balance_sequences(sl, 8)
+    flat = sorted(i for p in parts for i in p)
+    assert flat == list(range(256))
+    loads = [sum(sl[i] for i in p) for p in parts]
+    assert max(loads) - min(loads) <= max(sl)
+
+
+def test_head_shard():
+    assert shard.head_shard(32, 8, 8, 3) == (slice(12, 16), slice(3, 4))
+    with pytest.raises(ValueError):
+        shard.head_shard(32, 8, 3, 0)
+
+
+def test_slice_by_batch_keeps_only_own_pages():
+    x = W.make_gqa_inputs(W.CFG2_GQA_PAGED.scaled(batch=6, seqlen_lo=3, seqlen_hi=50), "cpu")
+    y = shard.slice_gqa_inputs_by_batch(x, [1, 4])
+    assert y["k_cache"].shape[0] == sum((int(l) + 15) // 16 for l in y["cache_seqlens"].tolist())
+    for j, b in enumerate([1, 4]):
+        n = (int(x["cache_seqlens"][b]) + 15) // 16
+        assert torch.equal(y["k_cache"][y["block_table"][j, :n].long()],
+                           x["k_cache"][x["block_table"][b, :n].long()])
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _gather_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        b, hq, d = 3, 8, 4
+        full = torch.arange(b * hq * d, dtype=torch.float32).view(b, hq, d)
+        lse_full = torch.arange(b * hq, dtype=torch.float32).view(b, hq)
+        qs, _ = shard.head_shard(hq, 4, world, rank)
+        out, lse = shard.gather_heads(full[:, qs].contiguous(), lse_full[:, qs].contiguous())
+        q.put((rank, bool(torch.equal(out, full) and torch.equal(lse, lse_full))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_head_gather_layout_gloo_world2():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(60)
+    res = dict(q.get(timeout=10) for _ in range(2))
+    assert res == {0: True, 1: True}
