@@ -126,6 +126,21 @@ int b2d_gqa_workspace_bytes(const b2d_gqa_args* args, size_t* bytes);
 int b2d_decode_gqa(const b2d_gqa_args* args, void* stream);
 
 /*
+ * Same decode as b2d_decode_gqa, for callers that cannot allocate device
+ * memory — e.g. a plugin whose enqueue step may not allocate, or a serving
+ * loop that reserved all free HBM for its KV cache at start-up — and so
+ * cannot pass a workspace.  No counterpart in the reference.  args->workspace
+ * and args->workspace_bytes are ignored: the scratch is a 16 MiB array of
+ * device memory inside this library, held on every GPU that loads it until
+ * the process exits.  Problems needing more than 16 MiB of workspace
+ * (b2d_gqa_workspace_bytes) return B2D_ERR_TOO_LARGE.  The first call on a
+ * device looks up the array's address and clears its status word (make it before any
+ * stream capture).  All calls share the array, so calls that overlap on the
+ * GPU race; serialise them.  Allocates nothing.
+ */
+int b2d_decode_gqa_static_scratch(const b2d_gqa_args* args, void* stream);
+
+/*
  * Absorbed-MLA decode (DeepSeek-V3 shape): every query head attends to one
  * shared latent KV head.  Scores use all head_dim_qk (= 576: 512 latent + 64
  * rope) columns; V is the first head_dim_v (= 512) columns of the same row.

@@ -16,6 +16,7 @@ B2D_FLAG_SKIP_COMBINE, B2D_FLAG_COMBINE_ONLY = 1, 2
 EXPORTED = (
     "b2d_gqa_workspace_bytes",
     "b2d_decode_gqa",
+    "b2d_decode_gqa_static_scratch",
     "b2d_mla_workspace_bytes",
     "b2d_decode_mla",
     "b2d_check_device_status",
@@ -79,6 +80,7 @@ def load() -> C.CDLL:
     lib = C.CDLL(str(path))
     lib.b2d_gqa_workspace_bytes.argtypes = [C.POINTER(GqaArgs), C.POINTER(C.c_size_t)]
     lib.b2d_decode_gqa.argtypes = [C.POINTER(GqaArgs), C.c_void_p]
+    lib.b2d_decode_gqa_static_scratch.argtypes = [C.POINTER(GqaArgs), C.c_void_p]
     lib.b2d_mla_workspace_bytes.argtypes = [C.POINTER(MlaArgs), C.POINTER(C.c_size_t)]
     lib.b2d_decode_mla.argtypes = [C.POINTER(MlaArgs), C.c_void_p]
     lib.b2d_check_device_status.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
