@@ -182,8 +182,9 @@ int b2d_decode_mla(const b2d_mla_args* args, void* stream);
  */
 int b2d_check_device_status(void* workspace, int clear, void* stream);
 
-/* Split plan the GQA kernel would use: number of CTAs and KV tokens per
- * pipeline chunk (host-only, no GPU access beyond a cached SM count). */
+/* Split plan the GQA kernel would use: number of CTAs (0 when num_ctas is 0:
+ * one resident wave, resolved at launch from the kernel's occupancy), KV
+ * tokens per pipeline chunk and KV heads per CTA (host-only). */
 int b2d_gqa_plan(const b2d_gqa_args* args, int32_t* num_ctas,
                  int32_t* chunk_tokens, int32_t* kv_heads_per_cta);
 

@@ -1,8 +1,11 @@
 // gqa_host.cu — host side of the GQA decode: argument validation, the split
 // plan, TMA descriptor encoding, workspace layout and the two launches.
 // Exposed through the C ABI in include/b2d_decode.h.
+#include <stdlib.h>
+
 #include "b2d_decode.h"
 #include "gqa_kernel.cuh"
+#include "gqa_mma_kernel.cuh"
 #include "host_common.h"
 
 namespace b2d {
@@ -10,11 +13,23 @@ namespace b2d {
 // Rows (sequence x KV-head group) handled by one launch; larger batches are
 // cut into slices of whole sequences that reuse the same workspace in order.
 constexpr int kMaxRowsPerLaunch = 2048;
-// Shared-memory budget for the K/V stage ring of one CTA (two CTAs per SM).
+// Default shared-memory budget for the K/V stage ring of one CTA.
 constexpr size_t kStageRingBytes = 96 * 1024;
 constexpr size_t kStatusBytes = 256;
+// Most resident CTAs per SM the workspace is sized for.
+constexpr int kMaxCtasPerSm = 4;
+
+// Tuning knobs read once from the environment (for measurement sweeps):
+// B2D_GQA_HQW caps the query heads per consumer warp (1, 2 or 4) and
+// B2D_GQA_RING_KB sets the stage-ring budget per CTA.
+static int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v ? atoi(v) : dflt;
+}
 
 struct GqaPlan {
+  bool mma;  // tensor-core consumer (page size % 16 == 0) or CUDA-core consumer
+  int np;    // mma: PV column tiles (1: <= 8 query heads per warp, 2: <= 16)
   int group, hqw, wph, hk, hg, nw, T, stages, ctas, rows_per_launch, seqs_per_launch;
   uint32_t stage_bytes;
   size_t smem;
@@ -64,39 +79,72 @@ static int validate(const b2d_gqa_args* a, bool need_pointers) {
 static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
   const int group = a->num_q_heads / a->num_kv_heads;
   pl->group = group;
-  pl->hqw = (group % 4 == 0) ? 4 : (group % 2 == 0 ? 2 : 1);
-  pl->wph = group / pl->hqw;
-  if (pl->wph > 8) return B2D_ERR_UNSUPPORTED;
-  pl->hk = largest_divisor_leq(a->num_kv_heads, 8 / pl->wph);
+  const int es = kv_elem_bytes(a->kv_dtype);
+  static const int use_mma = env_int("B2D_GQA_MMA", 1);
+  static const int hk_cap = env_int("B2D_GQA_HKMAX", 4);
+  // fp8 tiles use whole 128-byte lines per head row, so head_dim >= 128.
+  pl->mma = use_mma && (a->page_size % 16 == 0) &&
+            !(a->kv_dtype == B2D_FP8_E4M3 && a->head_dim < 128);
+  if (pl->mma) {
+    // Tensor-core consumer: a warp takes GW <= 16 query heads (<= 8 at
+    // head_dim 256, to bound the accumulator registers) of one KV head; a
+    // chunk is 16 tokens of HK KV heads.
+    const int gw_cap = a->head_dim == 256 ? 8 : 16;
+    int wph = 1;
+    while (group % wph != 0 || group / wph > gw_cap) ++wph;
+    pl->wph = wph;
+    pl->np = (group / wph) > 8 ? 2 : 1;
+    pl->hqw = group / wph;
+    if (wph > 8) return B2D_ERR_UNSUPPORTED;
+    int cap_hk = 8 / wph < hk_cap ? 8 / wph : hk_cap;
+    if (cap_hk < 1) cap_hk = 1;
+    pl->hk = largest_divisor_leq(a->num_kv_heads, cap_hk);
+    pl->T = 16;
+  } else {
+    static const int hqw_cap = env_int("B2D_GQA_HQW", 2);
+    pl->np = 0;
+    pl->hqw = (group % 4 == 0 && hqw_cap >= 4) ? 4 : (group % 2 == 0 && hqw_cap >= 2 ? 2 : 1);
+    pl->wph = group / pl->hqw;
+    if (pl->wph > 8) return B2D_ERR_UNSUPPORTED;
+    pl->hk = largest_divisor_leq(a->num_kv_heads, 8 / pl->wph);
+  }
   pl->hg = a->num_kv_heads / pl->hk;
   pl->nw = pl->hk * pl->wph;
-  const int es = kv_elem_bytes(a->kv_dtype);
   const int row_bytes = pl->hk * a->head_dim * es;
-  // Chunk: the largest divisor of the page size that keeps one K tile at
-  // <= 16 KB and the TMA box at <= 256 rows.
-  int tmax = 16384 / row_bytes;
-  if (tmax < 1) tmax = 1;
-  if (tmax > 256) tmax = 256;
-  pl->T = largest_divisor_leq(a->page_size, tmax);
+  if (!pl->mma) {
+    // Chunk: the largest divisor of the page size that keeps one K tile at
+    // <= 16 KB and the TMA box at <= 256 rows.
+    int tmax = 16384 / row_bytes;
+    if (tmax < 1) tmax = 1;
+    if (tmax > 256) tmax = 256;
+    pl->T = largest_divisor_leq(a->page_size, tmax);
+  }
   pl->stage_bytes = (uint32_t)(pl->T * row_bytes);
-  int stages = (int)(kStageRingBytes / (2 * (size_t)pl->stage_bytes));
+  static const size_t ring = (size_t)env_int("B2D_GQA_RING_KB", (int)(kStageRingBytes / 1024)) * 1024;
+  int stages = (int)(ring / (2 * (size_t)pl->stage_bytes));
   pl->stages = stages < 2 ? 2 : (stages > 8 ? 8 : stages);
   pl->seqs_per_launch = kMaxRowsPerLaunch / pl->hg;
   if (pl->seqs_per_launch < 1) return B2D_ERR_TOO_LARGE;
   if (pl->seqs_per_launch > a->batch) pl->seqs_per_launch = a->batch > 0 ? a->batch : 1;
   pl->rows_per_launch = pl->seqs_per_launch * pl->hg;
   pl->smem = (size_t)pl->stages * 2 * pl->stage_bytes + 2 * pl->stages * sizeof(uint64_t) +
-             (size_t)(pl->rows_per_launch + 1) * 4 + 32 * 4;
+             (size_t)(pl->rows_per_launch + 1) * 4 + 32 * 4 + (pl->mma ? 1024 : 0);
+  // Chunk indices are 32-bit in the kernel.
+  const int64_t max_chunks_per_row =
+      ((int64_t)a->max_pages_per_seq * a->page_size + pl->T - 1) / pl->T;
+  if (max_chunks_per_row * pl->rows_per_launch > (int64_t)INT32_MAX) return B2D_ERR_TOO_LARGE;
+  // num_ctas == 0: one resident wave, resolved at launch from the occupancy
+  // of the selected kernel; the workspace is sized for the largest wave.
   int ctas = a->num_ctas;
+  int ctas_cap = ctas;
   if (ctas <= 0) {
     int sms = 0;
     if (device_sm_count(&sms) != 0) return B2D_ERR_CUDA;
-    const int per_sm = (2 * (pl->smem + 1024) <= 227 * 1024) ? 2 : 1;
-    ctas = sms * per_sm;
+    ctas_cap = sms * kMaxCtasPerSm;
   }
   pl->ctas = ctas;
   const int hqc = pl->hk * group;
-  const size_t segs = (size_t)pl->rows_per_launch + ctas;
+  const size_t segs = (size_t)pl->rows_per_launch + ctas_cap;
   pl->off_row_start = kStatusBytes;
   pl->off_part_lse = align_up(pl->off_row_start + (size_t)(pl->rows_per_launch + 1) * 4, 256);
   pl->off_part_o = align_up(pl->off_part_lse + segs * hqc * 4, 256);
@@ -104,23 +152,54 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
   return B2D_OK;
 }
 
-template <int D, int KIND, typename QT, int HQW>
-static int launch_t(const GqaPlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
-                    const GqaParams& p, cudaStream_t st, int flags) {
-  auto kern = gqa_decode_kernel<D, KIND, QT, HQW>;
+template <typename Kern>
+static int launch_k(Kern kern, void (*combine)(const GqaParams, int), const GqaPlan& pl,
+                    const CUtensorMap& tk, const CUtensorMap& tv, const GqaParams& p,
+                    cudaStream_t st, int flags) {
+  const int threads = 32 * (pl.nw + 1);
+  if (ensure_dynamic_smem(reinterpret_cast<const void*>(kern), pl.smem)) return B2D_ERR_CUDA;
+  int ctas = pl.ctas;
+  if (ctas <= 0) {
+    int sms = 0, per_sm = 0;
+    if (device_sm_count(&sms) != 0) return B2D_ERR_CUDA;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, pl.smem) !=
+        cudaSuccess)
+      return B2D_ERR_CUDA;
+    per_sm = per_sm < 1 ? 1 : (per_sm > kMaxCtasPerSm ? kMaxCtasPerSm : per_sm);
+    ctas = sms * per_sm;
+  }
   if (!(flags & B2D_FLAG_COMBINE_ONLY)) {
-    if (ensure_dynamic_smem(reinterpret_cast<const void*>(kern), pl.smem)) return B2D_ERR_CUDA;
-    kern<<<pl.ctas, 32 * (pl.nw + 1), pl.smem, st>>>(tk, tv, p);
+    kern<<<ctas, threads, pl.smem, st>>>(tk, tv, p);
     if (cudaGetLastError() != cudaSuccess) return B2D_ERR_CUDA;
   }
   const int R = p.B * p.HG;
   const int64_t warps = (int64_t)R * pl.hk * pl.group;
   const int blocks = (int)((warps * 32 + 255) / 256);
   if (blocks > 0 && !(flags & B2D_FLAG_SKIP_COMBINE)) {
-    gqa_combine_kernel<D, QT><<<blocks, 256, 0, st>>>(p, pl.ctas);
+    combine<<<blocks, 256, 0, st>>>(p, ctas);
     if (cudaGetLastError() != cudaSuccess) return B2D_ERR_CUDA;
   }
   return B2D_OK;
+}
+
+template <int D, int KIND, typename QT, int HQW>
+static int launch_t(const GqaPlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
+                    const GqaParams& p, cudaStream_t st, int flags) {
+  return launch_k(gqa_decode_kernel<D, KIND, QT, HQW>, gqa_combine_kernel<D, QT>, pl, tk, tv, p,
+                  st, flags);
+}
+
+template <int D, int KIND, typename QT>
+static int launch_mma(const GqaPlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
+                      const GqaParams& p, cudaStream_t st, int flags) {
+  if (pl.np == 2) {
+    if constexpr (D == 256) return B2D_ERR_UNSUPPORTED;
+    else
+      return launch_k(gqa_mma_kernel<D, KIND, QT, 2>, gqa_combine_kernel<D, QT>, pl, tk, tv, p,
+                      st, flags);
+  }
+  return launch_k(gqa_mma_kernel<D, KIND, QT, 1>, gqa_combine_kernel<D, QT>, pl, tk, tv, p, st,
+                  flags);
 }
 
 template <int D, int KIND, typename QT>
@@ -138,6 +217,13 @@ static int launch_d(const b2d_gqa_args* a, const GqaPlan& pl, const CUtensorMap&
                     const CUtensorMap& tv, const GqaParams& p, cudaStream_t st) {
   const int flags = a->flags;
   const bool qbf = a->q_dtype == B2D_BF16;
+  if (pl.mma) {
+    if (a->kv_dtype == B2D_FP8_E4M3)
+      return qbf ? launch_mma<D, kKvFp8, __nv_bfloat16>(pl, tk, tv, p, st, flags)
+                 : launch_mma<D, kKvFp8, __half>(pl, tk, tv, p, st, flags);
+    return qbf ? launch_mma<D, kKvBf16, __nv_bfloat16>(pl, tk, tv, p, st, flags)
+               : launch_mma<D, kKvFp16, __half>(pl, tk, tv, p, st, flags);
+  }
   if (a->kv_dtype == B2D_FP8_E4M3) {
     return qbf ? launch_hqw<D, kKvFp8, __nv_bfloat16>(pl, tk, tv, p, st, flags)
                : launch_hqw<D, kKvFp8, __half>(pl, tk, tv, p, st, flags);
@@ -149,13 +235,25 @@ static int launch_d(const b2d_gqa_args* a, const GqaPlan& pl, const CUtensorMap&
 static int encode_kv_map(CUtensorMap* map, const void* base, const b2d_gqa_args* a,
                          int64_t s_page, int64_t s_tok, int64_t s_head, const GqaPlan& pl) {
   const int es = kv_elem_bytes(a->kv_dtype);
+  const CUtensorMapDataType dt = es == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  if (pl.mma) {
+    // {128-byte line, token, line of the head row, head, page}; 128-byte
+    // swizzle.  Shared layout: [HK][D / line][16 tokens][line].
+    const uint64_t line = 128 / es;
+    const uint64_t dims[5] = {line, (uint64_t)a->page_size, (uint64_t)a->head_dim / line,
+                              (uint64_t)a->num_kv_heads, (uint64_t)a->num_pages};
+    const uint64_t strides[4] = {(uint64_t)(s_tok * es), 128u, (uint64_t)(s_head * es),
+                                 (uint64_t)(s_page * es)};
+    const uint32_t box[5] = {(uint32_t)line, 16u, (uint32_t)(a->head_dim / line), (uint32_t)pl.hk,
+                             1u};
+    return encode_tiled_map(map, dt, 5, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   const uint64_t dims[4] = {(uint64_t)a->head_dim, (uint64_t)a->num_kv_heads,
                             (uint64_t)a->page_size, (uint64_t)a->num_pages};
   const uint64_t strides[3] = {(uint64_t)(s_head * es), (uint64_t)(s_tok * es),
                                (uint64_t)(s_page * es)};
   const uint32_t box[4] = {(uint32_t)a->head_dim, (uint32_t)pl.hk, (uint32_t)pl.T, 1u};
-  return encode_tiled_map(map, es == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
-                          4, base, dims, strides, box);
+  return encode_tiled_map(map, dt, 4, base, dims, strides, box);
 }
 
 }  // namespace b2d

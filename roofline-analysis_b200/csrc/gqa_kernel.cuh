@@ -237,17 +237,21 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
   // more each), so no segment id is ever left unwritten.
   const int G = W < (int64_t)gridDim.x ? (int)W : (int)gridDim.x;
   if (W == 0 || cta >= G) return;
-  const int64_t x0 = (int64_t)cta * W / G;
-  const int64_t x1 = (int64_t)(cta + 1) * W / G;
+  // Chunk indices fit in 32 bits (the host bounds W); only the range cut
+  // itself needs 64-bit products.
+  const int x0 = (int)((int64_t)cta * W / G);
+  const int x1 = (int)((int64_t)(cta + 1) * W / G);
   const int cap = p.max_pages * p.P;
 
   if (warp == p.NW) {
     // ---------------- producer warp ----------------
     const uint64_t policy = policy_evict_first();
     bool ok = true;
-    for (int64_t gbase = x0; gbase < x1 && ok; gbase += 32) {
+    int s = 0;
+    uint32_t ph = 0;
+    for (int gbase = x0; gbase < x1 && ok; gbase += 32) {
       // Each lane resolves one chunk's page id (coalesced block-table reads).
-      const int64_t x = gbase + lane;
+      const int x = gbase + lane;
       int my_page = 0, my_off = 0, my_h0 = 0;
       if (x < x1) {
         const int rr = find_row(row_start, R, x);
@@ -263,15 +267,12 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
         }
         my_page = pg;
       }
-      const int cnt = (x1 - gbase) < 32 ? (int)(x1 - gbase) : 32;
+      const int cnt = (x1 - gbase) < 32 ? (x1 - gbase) : 32;
       for (int k = 0; k < cnt; ++k) {
         const int page = __shfl_sync(0xffffffffu, my_page, k);
         const int off = __shfl_sync(0xffffffffu, my_off, k);
         const int h0 = __shfl_sync(0xffffffffu, my_h0, k);
         if (lane == 0 && ok) {
-          const int64_t i = gbase + k - x0;
-          const int s = (int)(i % p.stages);
-          const uint32_t ph = (uint32_t)((i / p.stages) & 1);
           if (!mbar_wait(empty + s, ph ^ 1u)) {
             record_status(p.status, kStatusTimeout);
             ok = false;
@@ -281,6 +282,10 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
             tma_load_4d(kdst, &tmap_k, full + s, 0, h0, off, page, policy);
             tma_load_4d(kdst + p.stage_bytes, &tmap_v, full + s, 0, h0, off, page, policy);
           }
+        }
+        if (++s == p.stages) {
+          s = 0;
+          ph ^= 1u;
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
       }
@@ -491,21 +496,20 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
   };
 
   int row = find_row(row_start, R, x0);
-  for (int64_t x = x0; x < x1; ++x) {
+  int s = 0;
+  uint32_t ph = 0;
+  for (int x = x0; x < x1; ++x) {
     while (x >= row_start[row + 1]) ++row;
     if (row != cur_row) {
       if (cur_row >= 0) finish_row(cur_row);
       start_row(row);
       cur_row = row;
     }
-    const int64_t i = x - x0;
-    const int s = (int)(i % p.stages);
-    const uint32_t ph = (uint32_t)((i / p.stages) & 1);
     if (!mbar_wait(full + s, ph)) {
       record_status(p.status, kStatusTimeout);
       return;
     }
-    const int tok0 = (int)(x - row_start[row]) * p.T;
+    const int tok0 = (x - row_start[row]) * p.T;
     const int nvalid = min(p.T, L - tok0);
     const uint32_t kbase = tiles_u32 + (uint32_t)s * 2u * p.stage_bytes + col_off;
     const uint32_t vbase = kbase + p.stage_bytes;
@@ -519,6 +523,10 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + s);
+    if (++s == p.stages) {
+      s = 0;
+      ph ^= 1u;
+    }
   }
   if (cur_row >= 0) finish_row(cur_row);
 }

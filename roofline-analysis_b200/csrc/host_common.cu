@@ -63,7 +63,8 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 int encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
-                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                     CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return -1;
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
@@ -71,7 +72,7 @@ int encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, cons
                   reinterpret_cast<const cuuint64_t*>(dims),
                   reinterpret_cast<const cuuint64_t*>(strides_bytes),
                   reinterpret_cast<const cuuint32_t*>(box), estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -1;
 }

@@ -19,9 +19,10 @@ int device_sm_count(int* sms);
 // least `bytes` (cached per device and function).  0 on success.
 int ensure_dynamic_smem(const void* func, size_t bytes);
 
-// cuTensorMapEncodeTiled with no interleave, no swizzle, 256-byte L2
+// cuTensorMapEncodeTiled with no interleave, the given swizzle, 256-byte L2
 // promotion and zero out-of-bounds fill.  0 on success.
 int encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
-                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box);
+                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                     CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
 }  // namespace b2d

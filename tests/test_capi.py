@@ -55,14 +55,19 @@ def test_workspace_query_and_plan_on_host():
     lib = _lib.load()
     n = C.c_size_t(0)
     assert lib.b2d_gqa_workspace_bytes(C.byref(_args()), C.byref(n)) == 0
-    # status + row_start + (rows + ctas) * heads * (D + 1) floats
-    assert n.value >= (64 + 296) * 32 * 129 * 4
     nc, t, hk = C.c_int32(), C.c_int32(), C.c_int32()
     assert lib.b2d_gqa_plan(C.byref(_args()), C.byref(nc), C.byref(t), C.byref(hk)) == 0
-    assert (nc.value, hk.value) == (296, 8) and 16 % t.value == 0
-    # GQA group 8 -> two warps per KV head, four KV heads per CTA
-    assert lib.b2d_gqa_plan(C.byref(_args(num_q_heads=64)), C.byref(nc), C.byref(t), C.byref(hk)) == 0
-    assert hk.value == 4
+    # status + row table + (rows + ctas) * (query heads per row) * (D + 1) floats
+    rows, heads_per_row = 64 * (8 // hk.value), 4 * hk.value
+    assert n.value >= (rows + 296) * heads_per_row * 129 * 4
+    assert nc.value == 296 and 16 % t.value == 0 and 8 % hk.value == 0
+    # page size 48: chunks still divide a page
+    assert lib.b2d_gqa_plan(C.byref(_args(page_size=48)), C.byref(nc), C.byref(t), C.byref(hk)) == 0
+    assert 48 % t.value == 0
+    # GQA group 8 and MQA group 32 are planned too
+    for hq in (64, 8 * 32):
+        assert lib.b2d_gqa_plan(C.byref(_args(num_q_heads=hq)), C.byref(nc), C.byref(t),
+                                C.byref(hk)) == 0
 
 
 @pytest.mark.parametrize("kw,code", [
