@@ -134,6 +134,16 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2_scaled(uint32_t w) {
   return mag | sgn;
 }
 
+// Two e4m3 bytes (low 16 bits of `w`) -> fp16x2 with the exact e4m3 values,
+// by the hardware conversion instruction.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2_cvt(uint32_t w) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 lo;\n\tcvt.u16.u32 lo, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, lo;\n\t}"
+      : "=r"(r)
+      : "r"(w));
+  return r;
+}
+
 __device__ __forceinline__ void record_status(int* status, int bits) {
   if (status != nullptr) atomicOr(status, bits);
 }

@@ -32,7 +32,22 @@
 
 #include "gqa_kernel.cuh"
 
+// FP8 fragments: hardware cvt (exact values) or the bit-move conversion
+// (values * 2^-8, folded into the scales).
+#ifndef B2D_FP8_HW_CVT
+#define B2D_FP8_HW_CVT 1
+#endif
+
 namespace b2d {
+
+__device__ __forceinline__ uint32_t fp8_pair(uint32_t w) {
+#if B2D_FP8_HW_CVT
+  return e4m3x2_to_f16x2_cvt(w);
+#else
+  return e4m3x2_to_f16x2_scaled(w);
+#endif
+}
+constexpr float kFp8FragScale = B2D_FP8_HW_CVT ? 1.f : 256.f;
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -222,8 +237,8 @@ __global__ void __launch_bounds__(32 * 9, 1)
     sc = p.scale_log2;
     vscale = 1.f;
     if constexpr (FP8) {
-      sc *= (p.k_scale ? __ldg(p.k_scale + kvh) : 1.f) * 256.f;
-      vscale = (p.v_scale ? __ldg(p.v_scale + kvh) : 1.f) * 256.f;
+      sc *= (p.k_scale ? __ldg(p.k_scale + kvh) : 1.f) * kFp8FragScale;
+      vscale = (p.v_scale ? __ldg(p.v_scale + kvh) : 1.f) * kFp8FragScale;
     }
     const int qh0 = kvh * p.group + qg * GW;
     const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)b * p.q_sb;
@@ -377,7 +392,7 @@ __global__ void __launch_bounds__(32 * 9, 1)
           const int dim = 16 * ks;
           const int line = line0 + (dim / LINE) * T + 8 * j + g;
           const uint32_t w = lds32(swz(kb, line, (dim % LINE) / 16) + 4 * t);
-          mma16816<false>(sfr[j], a, e4m3x2_to_f16x2_scaled(w), e4m3x2_to_f16x2_scaled(w >> 16));
+          mma16816<false>(sfr[j], a, fp8_pair(w), fp8_pair(w >> 16));
         }
       }
     }
@@ -467,10 +482,10 @@ __global__ void __launch_bounds__(32 * 9, 1)
           const uint32_t s0 = (2 * u) | ((4 + 2 * u) << 4);
           const uint32_t s1 = (2 * u + 1) | ((4 + 2 * u + 1) << 4);
           uint32_t afr[4];
-          afr[0] = e4m3x2_to_f16x2_scaled(__byte_perm(w0, w1, s0));
-          afr[1] = e4m3x2_to_f16x2_scaled(__byte_perm(w0, w1, s1));
-          afr[2] = e4m3x2_to_f16x2_scaled(__byte_perm(w2, w3, s0));
-          afr[3] = e4m3x2_to_f16x2_scaled(__byte_perm(w2, w3, s1));
+          afr[0] = fp8_pair(__byte_perm(w0, w1, s0));
+          afr[1] = fp8_pair(__byte_perm(w0, w1, s1));
+          afr[2] = fp8_pair(__byte_perm(w2, w3, s0));
+          afr[3] = fp8_pair(__byte_perm(w2, w3, s1));
 #pragma unroll
           for (int n = 0; n < NP; ++n) mma16816<false>(acc[n][2 * qd + u], afr, pb[n][0], pb[n][1]);
         }
