@@ -258,13 +258,17 @@ def main():
     sl = x["cache_seqlens"].cpu()
     local_bytes = W.gqa_algorithmic_bytes(w, sl)
 
-    def dec(**kw):
-        return b200decode.decode(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"],
-                                 x["block_table"], x["softmax_scale"], k_scale=x["k_scale"],
-                                 v_scale=x["v_scale"], **kw)
+    def make_decoder(flags=0, **kw):
+        # plan once, run every step (GqaDecoder is decode() with the argument
+        # checks hoisted out of the loop)
+        return b200decode.GqaDecoder(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"],
+                                     x["block_table"], x["softmax_scale"], k_scale=x["k_scale"],
+                                     v_scale=x["v_scale"], flags=flags, **kw)
+
+    decoder = make_decoder()
 
     def step():
-        out, lse = dec()
+        out, lse = decoder.run()
         if tp:
             out, lse = shard.gather_heads(out, lse)
         return out, lse
@@ -303,17 +307,30 @@ def main():
 
     # ---- the split-KV kernel and the combine kernel alone ----
     def timed(flag, n):
+        d = make_decoder(flag)
         for _ in range(3):
-            dec(flags=flag)
+            d.run()
         torch.cuda.synchronize()
         ev0.record(stream)
         for _ in range(n):
-            dec(flags=flag)
+            d.run()
         ev1.record(stream)
         torch.cuda.synchronize()
         return ev0.elapsed_time(ev1) / n
 
     kk = max(5, args.steps)
+    graph_ms = None
+    if not tp:
+        gdec = make_decoder().capture()
+        for _ in range(3):
+            gdec.replay()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(kk):
+            gdec.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        graph_ms = ev0.elapsed_time(ev1) / kk
     kern_ms = timed(_lib.B2D_FLAG_SKIP_COMBINE, kk)
     combine_ms = timed(_lib.B2D_FLAG_COMBINE_ONLY, kk)
     peak, peak_kind = measured_hbm_peak()
@@ -331,13 +348,15 @@ def main():
         out_h = torch.empty((w.batch, hq_out, w.head_dim), dtype=x["q"].dtype).pin_memory()
         lse_h = torch.empty((w.batch, hq_out), dtype=torch.float32).pin_memory()
 
+        e2e_dec = b200decode.GqaDecoder(qd, x["k_cache"], x["v_cache"], sld, btd,
+                                        x["softmax_scale"], k_scale=x["k_scale"],
+                                        v_scale=x["v_scale"])
+
         def e2e_step():
             qd.copy_(qh, non_blocking=True)
             sld.copy_(slh, non_blocking=True)
             btd.copy_(bth, non_blocking=True)
-            out, lse = b200decode.decode(qd, x["k_cache"], x["v_cache"], sld, btd,
-                                         x["softmax_scale"], k_scale=x["k_scale"],
-                                         v_scale=x["v_scale"])
+            out, lse = e2e_dec.run()
             if tp:
                 out, lse = shard.gather_heads(out, lse)
             out_h.copy_(out, non_blocking=True)
@@ -401,6 +420,7 @@ def main():
                          "traffic": committed_traffic(w0.name),
                          "kernel_us": round(kern_ms * 1e3, 2),
                          "combine_us": round(combine_ms * 1e3, 2),
+                         "cuda_graph_step_us": None if graph_ms is None else round(graph_ms * 1e3, 2),
                          "bytes_per_launch": int(local_bytes)},
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -14,6 +14,7 @@ library or without a CUDA device raises.
 from .api import (  # noqa: F401
     B2DError,
     DecodeWorkspace,
+    GqaDecoder,
     check_device_status,
     decode,
     decode_mla,

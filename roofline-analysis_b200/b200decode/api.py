@@ -182,6 +182,68 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     return out, lse
 
 
+class GqaDecoder:
+    """Plan once, run many times: the plan()/run() split of FlashInfer's
+    BatchDecodeWithPagedKVCacheWrapper (decodebench/flashinfer_kernel.py:
+    88-116), so a decode loop pays the argument checks and workspace sizing
+    once.  Tensors are bound by address: refill q / cache_seqlens /
+    block_table / the caches in place between runs (shapes fixed).
+
+    run() enqueues one decode on the current stream and returns (out, lse).
+    capture() records run() into a CUDA graph; replay() launches it.
+    """
+
+    def __init__(self, q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale=None, *,
+                 k_scale=None, v_scale=None, out=None, lse=None, kv_layout="NHD",
+                 num_ctas=None, workspace=None, flags=0):
+        if not q.is_cuda:
+            raise RuntimeError("GqaDecoder needs CUDA tensors (there is no CPU path)")
+        self._lib = _lib.load()
+        q3 = q[:, 0] if q.dim() == 4 else q
+        if softmax_scale is None:
+            softmax_scale = q3.shape[-1] ** -0.5
+        self.out = torch.empty_like(q) if out is None else out
+        out3 = self.out[:, 0] if self.out.dim() == 4 else self.out
+        self.lse = (torch.empty(q3.shape[0], q3.shape[1], dtype=torch.float32, device=q.device)
+                    if lse is None else lse)
+        self._args = _gqa_args(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale,
+                               k_scale, v_scale, out3, self.lse, kv_layout, num_ctas)
+        self._args.flags = int(flags)
+        self._keep = (q, k_cache, v_cache, cache_seqlens, block_table, k_scale, v_scale)
+        self.ws = workspace or _default_ws(q.device)
+        need = C.c_size_t(0)
+        _check(self._lib.b2d_gqa_workspace_bytes(C.byref(self._args), C.byref(need)),
+               "b2d_gqa_workspace_bytes")
+        self.ws.ensure(need.value)
+        self._ws_buf = self.ws.buf   # pin the buffer this plan points at
+        self._args.workspace, self._args.workspace_bytes = self.ws.ptr, self.ws.nbytes
+        self._argp = C.byref(self._args)
+        self._fn = self._lib.b2d_decode_gqa
+        self.device = q.device
+        self._graph = None
+
+    def run(self):
+        rc = self._fn(self._argp, C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        if rc:
+            raise B2DError(rc, "b2d_decode_gqa")
+        return self.out, self.lse
+
+    def capture(self):
+        """Record one run() into a CUDA graph (after a warm-up run, which does
+        the one-time per-device set-up outside the capture)."""
+        self.run()
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.run()
+        self._graph = g
+        return self
+
+    def replay(self):
+        self._graph.replay()
+        return self.out, self.lse
+
+
 def gqa_plan(q, k_cache, v_cache, cache_seqlens, block_table, kv_layout="NHD", num_ctas=None):
     """(num_ctas, chunk_tokens, kv_heads_per_cta) the kernel would use."""
     lib = _lib.load()

@@ -162,8 +162,7 @@ static int launch_k(Kern kern, void (*combine)(const GqaParams, int), const GqaP
   if (ctas <= 0) {
     int sms = 0, per_sm = 0;
     if (device_sm_count(&sms) != 0) return B2D_ERR_CUDA;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, pl.smem) !=
-        cudaSuccess)
+    if (occupancy_per_sm(reinterpret_cast<const void*>(kern), threads, pl.smem, &per_sm))
       return B2D_ERR_CUDA;
     per_sm = per_sm < 1 ? 1 : (per_sm > kMaxCtasPerSm ? kMaxCtasPerSm : per_sm);
     ctas = sms * per_sm;

@@ -3,6 +3,7 @@
 
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 namespace b2d {
@@ -40,6 +41,23 @@ int ensure_dynamic_smem(const void* func, size_t bytes) {
                            cudaSharedmemCarveoutMaxShared) != cudaSuccess)
     return -1;
   done[key] = bytes;
+  return 0;
+}
+
+int occupancy_per_sm(const void* func, int threads, size_t smem, int* per_sm) {
+  static std::map<std::tuple<const void*, int, int, size_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  std::lock_guard<std::mutex> g(g_mu);
+  auto key = std::make_tuple(func, dev, threads, smem);
+  auto it = cache.find(key);
+  if (it == cache.end()) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, smem) != cudaSuccess)
+      return -1;
+    it = cache.emplace(key, n).first;
+  }
+  *per_sm = it->second;
   return 0;
 }
 

@@ -19,6 +19,10 @@ int device_sm_count(int* sms);
 // least `bytes` (cached per device and function).  0 on success.
 int ensure_dynamic_smem(const void* func, size_t bytes);
 
+// Resident CTAs per SM of `func` at this block size and dynamic shared
+// memory on the current device (cached).  0 on success.
+int occupancy_per_sm(const void* func, int threads, size_t smem, int* per_sm);
+
 // cuTensorMapEncodeTiled with no interleave, the given swizzle, 256-byte L2
 // promotion and zero out-of-bounds fill.  0 on success.
 int encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,

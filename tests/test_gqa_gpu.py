@@ -192,3 +192,20 @@ def test_cfg3_long_context_full(cuda):
     out2, lse2 = _run(x, num_ctas=37)
     assert (out2.float() - out.float()).abs().max().item() < 1e-2
     assert (lse2 - lse).abs().max().item() < 1e-4
+
+
+def test_decoder_plan_run_and_graph_replay(cuda):
+    """Plan/run object and its CUDA-graph replay give the decode() result,
+    and pick up in-place refills of q and the lengths."""
+    x = _inputs(cuda, SMALL.scaled(batch=6, seqlen_hi=900))
+    dec = b200decode.GqaDecoder(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"],
+                                x["block_table"], x["softmax_scale"])
+    out, lse = dec.run()
+    torch.cuda.synchronize()
+    assert_parity(out, lse, *oracle_gqa(x))
+    dec.capture()
+    x["q"].copy_(torch.randn_like(x["q"], dtype=torch.float32).to(x["q"].dtype))
+    x["cache_seqlens"].copy_(torch.clamp(x["cache_seqlens"] - 7, min=0))
+    out, lse = dec.replay()
+    torch.cuda.synchronize()
+    assert_parity(out, lse, *oracle_gqa(x))
