@@ -221,11 +221,10 @@ def main():
     w0 = W.get(args.workload)
     if args.batch:
         w0 = w0.scaled(batch=args.batch)
-    if not isinstance(w0, W.GqaWorkload):
-        raise SystemExit("bench.py measures the GQA decode workloads (cfg1/cfg2/cfg3/cfg5)")
-
     if args.impl == "reference":
         return run_reference_arm(args, world, rank, w0)
+    if isinstance(w0, W.MlaWorkload):
+        return run_mla(args, world, rank, local, w0)
 
     import b200decode
     from b200decode import _lib, shard
@@ -433,6 +432,190 @@ def main():
         dist.destroy_process_group()
 
 
+def measured_bf16_peak():
+    try:
+        d = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+        return float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def mla_cpu_sample(x, n, scale):
+    """First n MLA sequences as dense CPU tensors -> (q [n,128,576], [(kv [1,1,L,576])])."""
+    sl = x["cache_seqlens"][:n].cpu().tolist()
+    bt = x["block_table"][:n].cpu()
+    page = x["kv_cache"].shape[1]
+    dense = []
+    for b, length in enumerate(sl):
+        npg = (length + page - 1) // page
+        kv = x["kv_cache"][bt[b, :npg].long().to(x["kv_cache"].device)].reshape(-1, 576)[:length]
+        dense.append(kv.cpu()[None, None])
+    return x["q"][:n].cpu(), dense
+
+
+def mla_cpu_decode(q, dense, scale):
+    import torch.nn.functional as F
+    outs = []
+    for b, kv in enumerate(dense):
+        qb = q[b:b + 1, :, None, :]
+        o = F.scaled_dot_product_attention(qb, kv, kv[..., :512], is_causal=False, scale=scale,
+                                           enable_gqa=True)
+        outs.append(o[:, :, 0])
+    return torch.cat(outs)
+
+
+def run_mla(args, world, rank, local, w0):
+    """Absorbed-MLA decode; weak scaling across ranks."""
+    import b200decode
+    from b200decode import _lib
+    from b200decode import workloads as W
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    SUM, MAX = dist.ReduceOp.SUM, dist.ReduceOp.MAX
+    w = w0.scaled(seed=w0.seed + rank) if world > 1 else w0
+    x = W.make_mla_inputs(w, dev)
+    sl = x["cache_seqlens"].cpu()
+    local_bytes = W.mla_algorithmic_bytes(w, sl)
+    local_flops = W.mla_flops(w, sl)
+    out = torch.empty(w.batch, w.num_heads, w.head_dim_v, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(w.batch, w.num_heads, dtype=torch.float32, device=dev)
+
+    def dec(flags=0, q=None, seqlens=None, bt=None):
+        return b200decode.decode_mla(x["q"] if q is None else q, x["kv_cache"],
+                                     x["cache_seqlens"] if seqlens is None else seqlens,
+                                     x["block_table"] if bt is None else bt, x["softmax_scale"],
+                                     out=out, lse=lse, flags=flags)
+
+    for _ in range(max(3, args.warmup)):
+        dec()
+    torch.cuda.synchronize()
+    b200decode.check_device_status()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            dec()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = reduce_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, dev, MAX)
+
+    def timed(flag):
+        for _ in range(3):
+            dec(flag)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            dec(flag)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) / args.steps
+
+    kern_ms = timed(_lib.B2D_FLAG_SKIP_COMBINE)
+    combine_ms = timed(_lib.B2D_FLAG_COMBINE_ONLY)
+    total_bytes = reduce_over_ranks(local_bytes, world, dev, SUM)
+    total_flops = reduce_over_ranks(local_flops, world, dev, SUM)
+    hbm_peak, hbm_kind = measured_hbm_peak()
+    tc_peak, tc_kind = measured_bf16_peak()
+    ach_gbs = local_bytes / (kern_ms * 1e-3) / 1e9
+    ach_tfs = local_flops / (kern_ms * 1e-3) / 1e12
+    t_hbm = local_bytes / (hbm_peak * 1e9)
+    t_tc = local_flops / (tc_peak * 1e12)
+    bound = "hbm" if t_hbm >= t_tc else "tensor"
+
+    e2e = None
+    if not args.no_e2e:
+        qh = x["q"].cpu().pin_memory()
+        slh = x["cache_seqlens"].cpu().pin_memory()
+        bth = x["block_table"].cpu().pin_memory()
+        qd, sld, btd = torch.empty_like(x["q"]), torch.empty_like(x["cache_seqlens"]), torch.empty_like(x["block_table"])
+        out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        lse_h = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
+
+        def e2e_step():
+            qd.copy_(qh, non_blocking=True)
+            sld.copy_(slh, non_blocking=True)
+            btd.copy_(bth, non_blocking=True)
+            dec(0, qd, sld, btd)
+            out_h.copy_(out, non_blocking=True)
+            lse_h.copy_(lse, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = reduce_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, dev, MAX)
+        h2d = qh.numel() * 2 + slh.numel() * 4 + bth.numel() * 4
+        d2h = out_h.numel() * 2 + lse_h.numel() * 4
+        e2e = {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+               "us_per_step": round(e2e_ms * 1e3, 2),
+               "h2d_bytes_per_step": int(reduce_over_ranks(h2d, world, dev, SUM)),
+               "d2h_bytes_per_step": int(reduce_over_ranks(d2h, world, dev, SUM))}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        q_s, dense = mla_cpu_sample(x, 1, x["softmax_scale"])
+        torch.set_num_threads(os.cpu_count() or 1)
+        mla_cpu_decode(q_s, dense, x["softmax_scale"])
+        times = []
+        t_end = time.perf_counter() + args.cpu_seconds
+        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 200):
+            t0 = time.perf_counter()
+            mla_cpu_decode(q_s, dense, x["softmax_scale"])
+            times.append(time.perf_counter() - t0)
+        sec = statistics.median(times)
+        sb = W.mla_algorithmic_bytes(w.scaled(batch=1), sl[:1])
+        cpu = {"value": round(sb / sec / 1e12, 6), "unit": "TB/s", "cores": torch.get_num_threads(),
+               "kind": "reference",
+               "sample": (f"torch SDPA on CPU (the decode call of decodebench/torch_sdpa_benchmark.py:"
+                          f"100-102 with enable_gqa, one 576-wide latent KV head, V = first 512 "
+                          f"columns) over the first of {w.batch} sequences ({int(sl[0])} tokens); "
+                          f"median of {len(times)} passes, {sec * 1e3:.1f} ms each"),
+               "cpu_model": cpu_model(), "os_cpu_count": os.cpu_count()}
+
+    if rank == 0:
+        tbs = total_bytes / (ms * 1e-3) / 1e12
+        line = {
+            "metric": METRIC, "value": round(tbs, 4), "unit": "TB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
+            "us_per_step": round(ms * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "pct_hbm_roofline": round(100 * tbs / (hbm_peak * world / 1e3), 2),
+            "dtype": "bf16 in, fp32 accumulate (tcgen05)",
+            "data": "synthetic: seeded N(0, 0.5) q and latent cache, lengths ~ U[%d,%d], random page permutation" % (w0.seqlen_lo, w0.seqlen_hi),
+            "config": {"workload": w0.name, "batch": w0.batch, "num_heads": w0.num_heads,
+                       "head_dim_qk": w0.head_dim_qk, "head_dim_v": w0.head_dim_v,
+                       "page_size": w0.page_size, "parallelism": f"dp{world}-weak" if world > 1 else "single",
+                       "tokens_per_step": int(reduce_over_ranks(int(sl.sum()), world, dev, SUM)),
+                       "algorithmic_bytes_per_step": int(total_bytes), "flops_per_step": int(total_flops),
+                       "l2": "each step reads >1 GB of latent cache (> 126 MB L2); no flush"},
+            "roofline": {"bound": bound, "kernel": "b2d::mla_decode_kernel",
+                         "achieved": round(ach_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(max(t_hbm, t_tc) / (kern_ms * 1e-3), 4),
+                         "peak_source": hbm_kind,
+                         "tensor": {"achieved": round(ach_tfs, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                                    "frac": round(ach_tfs / tc_peak, 4), "peak_source": tc_kind},
+                         "traffic": committed_traffic(w0.name), "kernel_us": round(kern_ms * 1e3, 2),
+                         "combine_us": round(combine_ms * 1e3, 2), "bytes_per_launch": int(local_bytes)},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_reference_arm(args, world, rank, w0):
     """The reference's CPU decode path (torch SDPA on host cores), timed on
     rank 0 only, each step a bounded sample of the same workload."""
@@ -440,6 +623,8 @@ def run_reference_arm(args, world, rank, w0):
         return
     from b200decode import workloads as W
     from oracle.sdpa_cpu import sdpa_decode
+    if isinstance(w0, W.MlaWorkload):
+        raise SystemExit("--impl reference times the GQA configurations")
     torch.set_num_threads(os.cpu_count() or 1)
     seqlens = W.draw_seqlens(w0.batch, w0.seqlen_lo, w0.seqlen_hi, w0.seed)
     budget = max(0.2, 120.0 / (args.steps + max(3, args.warmup)))

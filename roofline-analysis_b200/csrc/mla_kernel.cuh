@@ -64,14 +64,19 @@ constexpr int kStages = 3;
 constexpr uint32_t kQBytes = kCB * kHeads * 128;     // 73728
 constexpr uint32_t kStageBytes = kCB * kT * 128;     // 36864
 constexpr uint32_t kPBytes = kHeads * 128;           // 8192 (32 tokens used of 64)
+constexpr int kSplit = 1;          // independent QK accumulators per score tile
+constexpr int kSBuf = 2;           // score tiles in TMEM (lane half 0, columns 256 + 128k)
+constexpr int kPBuf = 3;           // P tiles in shared memory
+constexpr int kAhead = 1;          // QK tiles issued ahead of the oldest pending P.V
 constexpr float kLazy = 8.f;                         // lazy-rescale threshold, log2 units
 constexpr int kThreads = 6 * 32;
 // shared-memory map (offsets from the 1024-aligned base)
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffKV = kOffQ + kQBytes;
 constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;
-constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
-constexpr uint32_t kNumBars = 2 * kStages + 2 + 2 + 2 + 2 + 2;  // kv f/e, q f/e, s f, p f, pv done, o f/e
+constexpr uint32_t kOffBar = kOffP + kPBuf * kPBytes;
+// kv full/empty, q full/empty, s full, p full, pv done, o full/empty
+constexpr uint32_t kNumBars = 2 * kStages + 2 + kSBuf + kPBuf + kPBuf + 2;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffRows = kOffTmem + 16;
 }  // namespace mla
@@ -193,10 +198,10 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
   uint64_t* kv_empty = bars + kStages;
   uint64_t* q_full = bars + 2 * kStages;
   uint64_t* q_empty = q_full + 1;
-  uint64_t* s_full = q_full + 2;      // [2]
-  uint64_t* p_full = s_full + 2;      // [2]
-  uint64_t* pv_done = p_full + 2;     // [2]
-  uint64_t* o_full = pv_done + 2;
+  uint64_t* s_full = q_full + 2;      // [kSBuf]
+  uint64_t* p_full = s_full + kSBuf;  // [kPBuf]
+  uint64_t* pv_done = p_full + kPBuf; // [kPBuf]
+  uint64_t* o_full = pv_done + kPBuf;
   uint64_t* o_empty = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
   int32_t* row_start = reinterpret_cast<int32_t*>(smem + kOffRows);
@@ -215,8 +220,8 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
     }
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int j = 0; j < 2; ++j) {
-      mbar_init(s_full + j, 1);
+    for (int j = 0; j < kSBuf; ++j) mbar_init(s_full + j, 1);
+    for (int j = 0; j < kPBuf; ++j) {
       mbar_init(p_full + j, 128);
       mbar_init(pv_done + j, 1);
     }
@@ -299,30 +304,55 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
       int row = find_row(row_start, R, x0);
       int cur = -1, nq = 0, nrow = 0, s = 0;
       uint32_t ph = 0;
-      int prev = -1, prev_stage = 0;
-      bool prev_first = false;
       bool ok = true;
       auto issue_pv = [&](int j, int stage, bool first_of_row) -> bool {
-        if (!mla_wait(p_full + (j & 1), (uint32_t)((j >> 1) & 1), p.status)) return false;
+        if (!mla_wait(p_full + j % kPBuf, (uint32_t)((j / kPBuf) & 1), p.status)) return false;
         if (first_of_row && nrow > 1) {
           if (!mla_wait(o_empty, (uint32_t)((nrow - 2) & 1), p.status)) return false;
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t pa = sbase + kOffP + (j & 1) * kPBytes;
+          const uint32_t pa = sbase + kOffP + (j % kPBuf) * kPBytes;
           const uint32_t vb = sbase + kOffKV + stage * kStageBytes;
 #pragma unroll
+          const uint64_t pd0 = umma_desc_sw128(pa, 16, 1024);
+          const uint64_t vd0 = umma_desc_sw128(vb, kT * 128, 1024);
           for (int ks = 0; ks < kT / 16; ++ks) {
-            const uint64_t ad = umma_desc_sw128(pa + ks * 32, 16, 1024);
+            const uint64_t ad = pd0 + (uint64_t)((ks * 32) >> 4);
 #pragma unroll
             for (int hv = 0; hv < 2; ++hv) {
-              const uint64_t bd = umma_desc_sw128(vb + hv * 4 * (kT * 128) + ks * 16 * 128,
-                                                  kT * 128, 1024);
+              const uint64_t bd = vd0 + (uint64_t)((hv * 4 * (kT * 128) + ks * 16 * 128) >> 4);
               umma_bf16(t_o + ((uint32_t)hv << 20), ad, bd, idesc_pv, !(first_of_row && ks == 0));
             }
           }
           umma_commit(kv_empty + stage);
-          umma_commit(pv_done + (j & 1));
+          umma_commit(pv_done + j % kPBuf);
+        }
+        __syncwarp();
+        return true;
+      };
+      // Chunks whose QK is issued but whose P.V is not (a short FIFO): QK runs
+      // kAhead chunks ahead so the tensor pipe has work while the softmax
+      // warps turn S(i) into P(i).
+      int pend_i[kAhead + 1], pend_s[kAhead + 1];
+      bool pend_f[kAhead + 1];
+      int np = 0;
+      auto pop_pv = [&]() -> bool {
+        const bool r = issue_pv(pend_i[0], pend_s[0], pend_f[0]);
+        for (int k = 1; k < np; ++k) {
+          pend_i[k - 1] = pend_i[k];
+          pend_s[k - 1] = pend_s[k];
+          pend_f[k - 1] = pend_f[k];
+        }
+        --np;
+        return r;
+      };
+      auto drain_row = [&]() -> bool {
+        while (np > 0)
+          if (!pop_pv()) return false;
+        if (lane == 0) {
+          umma_commit(o_full);
+          umma_commit(q_empty);
         }
         __syncwarp();
         return true;
@@ -332,56 +362,43 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         while (x >= row_start[row + 1]) ++row;
         const bool first = row != cur;
         if (first) {
-          if (prev >= 0) {
-            ok = issue_pv(prev, prev_stage, prev_first);
-            if (!ok) break;
-            if (lane == 0) {
-              umma_commit(o_full);
-              umma_commit(q_empty);
-            }
-            __syncwarp();
-            prev = -1;
-          }
+          if (cur >= 0 && !(ok = drain_row())) break;
           cur = row;
           ++nrow;
-          if (!mla_wait(q_full, (uint32_t)(nq & 1), p.status)) break;
+          if (!mla_wait(q_full, (uint32_t)(nq & 1), p.status)) { ok = false; break; }
           ++nq;
         }
-        if (!mla_wait(kv_full + s, ph, p.status)) break;
+        if (!mla_wait(kv_full + s, ph, p.status)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
           const uint32_t kb = sbase + kOffKV + s * kStageBytes;
           const uint32_t qb = sbase + kOffQ;
-          const uint32_t ts = t_s + (i & 1) * kT;
-#pragma unroll 4
+          const uint32_t ts = t_s + (uint32_t)((i % kSBuf) * kSplit * kT);
+          // Descriptors differ from the tile bases only in the start-address
+          // field (16-byte units), so each k-step adds a constant.
+          const uint64_t ad0 = umma_desc_sw128(qb, 16, 1024);
+          const uint64_t bd0 = umma_desc_sw128(kb, 16, 1024);
+#pragma unroll
           for (int kk = 0; kk < kDqk / 16; ++kk) {
             const int cb = kk >> 2, ko = (kk & 3) * 32;
-            const uint64_t ad = umma_desc_sw128(qb + cb * (kHeads * 128) + ko, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(kb + cb * (kT * 128) + ko, 16, 1024);
-            umma_bf16(ts, ad, bd, idesc_qk, kk > 0);
+            const uint64_t ad = ad0 + (uint64_t)((cb * (kHeads * 128) + ko) >> 4);
+            const uint64_t bd = bd0 + (uint64_t)((cb * (kT * 128) + ko) >> 4);
+            umma_bf16(ts + (uint32_t)((kk % kSplit) * kT), ad, bd, idesc_qk, kk >= kSplit);
           }
-          umma_commit(s_full + (i & 1));
+          umma_commit(s_full + i % kSBuf);
         }
         __syncwarp();
-        if (prev >= 0) {
-          ok = issue_pv(prev, prev_stage, prev_first);
-          if (!ok) break;
-        }
-        prev = i;
-        prev_stage = s;
-        prev_first = first;
+        pend_i[np] = i;
+        pend_s[np] = s;
+        pend_f[np] = first;
+        ++np;
+        while (np > kAhead && ok) ok = pop_pv();
         if (++s == kStages) {
           s = 0;
           ph ^= 1u;
         }
       }
-      if (ok && prev >= 0) {
-        if (issue_pv(prev, prev_stage, prev_first) && lane == 0) {
-          umma_commit(o_full);
-          umma_commit(q_empty);
-        }
-        __syncwarp();
-      }
+      if (ok && cur >= 0) drain_row();
     }
   } else {
     // ---------------- softmax + epilogue (warps 0-3) ----------------
@@ -411,10 +428,17 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         const int nvalid = min(kT, L - tok0);
         const int stage = i % kStages;
 
-        if (!mla_wait(s_full + (i & 1), (uint32_t)((i >> 1) & 1), p.status)) { ok = false; break; }
+        if (!mla_wait(s_full + i % kSBuf, (uint32_t)((i / kSBuf) & 1), p.status)) { ok = false; break; }
         tc_fence_after();
         float sv[kT];
-        tmem_ld32(t_warp + 256u + (uint32_t)((i & 1) * kT), sv);
+        tmem_ld32(t_warp + 256u + (uint32_t)((i % kSBuf) * kSplit * kT), sv);
+#pragma unroll
+        for (int part = 1; part < kSplit; ++part) {
+          float sp[kT];
+          tmem_ld32(t_warp + 256u + (uint32_t)(((i % kSBuf) * kSplit + part) * kT), sp);
+#pragma unroll
+          for (int t = 0; t < kT; ++t) sv[t] += sp[t];
+        }
         // Lanes >= 16 read unused columns of lane half 1 here; lanes < 16 hold the S row.
         float cm = -INFINITY;
 #pragma unroll
@@ -435,7 +459,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         const float alpha_o = __shfl_sync(0xffffffffu, alpha, lane & 15);
         if (any_need && !first_chunk) {
           // O must be complete up to the previous chunk before it is rescaled.
-          if (!mla_wait(pv_done + ((i - 1) & 1), (uint32_t)(((i - 1) >> 1) & 1), p.status)) { ok = false; break; }
+          if (!mla_wait(pv_done + (i - 1) % kPBuf, (uint32_t)(((i - 1) / kPBuf) & 1), p.status)) { ok = false; break; }
           tc_fence_after();
           for (int c = 0; c < kDv / 2; c += 32) {
             float ov[32];
@@ -447,10 +471,10 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           tc_fence_before();
         }
         // P row (bf16) into the swizzled K-major P buffer; P(i-2) must be consumed.
-        if (i >= 2) {
-          if (!mla_wait(pv_done + (i & 1), (uint32_t)(((i - 2) >> 1) & 1), p.status)) { ok = false; break; }
+        if (i >= kPBuf) {
+          if (!mla_wait(pv_done + i % kPBuf, (uint32_t)(((i - kPBuf) / kPBuf) & 1), p.status)) { ok = false; break; }
         }
-        uint8_t* pbuf = smem + kOffP + (i & 1) * kPBytes;
+        uint8_t* pbuf = smem + kOffP + (i % kPBuf) * kPBytes;
         if (s_lane) {
           float psum = 0.f;
           uint32_t pk[kT / 2];
@@ -484,7 +508,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         }
         fence_async_smem();
         tc_fence_before();
-        mbar_arrive(p_full + (i & 1));
+        mbar_arrive(p_full + i % kPBuf);
 
         if (last) {
           if (!mla_wait(o_full, (uint32_t)((nrow - 1) & 1), p.status)) { ok = false; break; }
