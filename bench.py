@@ -122,7 +122,7 @@ class ClockSampler:
     def _run(self):
         while not self._stop.is_set():
             self._sample()
-            time.sleep(0.02)
+            time.sleep(0.001)
 
     def __enter__(self):
         if self.nv is not None:
@@ -413,7 +413,9 @@ def main():
                        "flops_per_step": int(total_flops),
                        "l2": "each step reads >1 GB of KV (> 126 MB L2); no flush between steps",
                        "num_ctas": n_ctas, "chunk_tokens": chunk, "kv_heads_per_cta": hk_cta},
-            "roofline": {"bound": "hbm", "kernel": "b2d::gqa_decode_kernel",
+            "roofline": {"bound": "hbm",
+                         "kernel": "b2d::gqa_mma_kernel" if w0.page_size % 16 == 0 and not (
+                             w0.kv_dtype == "fp8" and w0.head_dim < 128) else "b2d::gqa_decode_kernel",
                          "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved_gbs / peak, 4), "peak_source": peak_kind,
                          "traffic": committed_traffic(w0.name),
