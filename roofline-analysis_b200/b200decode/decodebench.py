@@ -1,0 +1,196 @@
+"""decodebench backend "b2d_decode": the adapter pair the reference's harness
+expects (decodebench/<x>_kernel.py + <x>_benchmark.py), for this library.
+
+Kernel side mirrors decodebench/flashinfer_kernel.py:41-116: the constructor
+builds q, the paged caches, the lengths and the block table for a shape (the
+reference's DecodeShape fields, decodebench/flashinfer_kernel.py:8-28), and
+run() is the single timed call.  Benchmark side mirrors
+decodebench/flashinfer_benchmark.py:17-103: warm-up, one CUDA-event pair per
+run(), p50/p95/avg, and the same JSON record, extended with this library's
+fields (lengths distribution, seed, roofline figures).
+
+    python -m b200decode.decodebench --batch-size 64 --context-len 4096 \\
+        --num-q-heads 32 --num-kv-heads 8 --head-dim 128 --kv-dtype bf16 \\
+        --page-size 16 --output result.json [--seqlen-lo 1024 --seqlen-hi 8192]
+"""
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import json
+import math
+import os
+from datetime import datetime, timezone
+from pathlib import Path
+from typing import Optional
+
+import torch
+
+from . import api
+from . import workloads as W
+
+
+@dataclasses.dataclass(frozen=True)
+class DecodeShape:
+    """Field-for-field the reference's record (flashinfer_kernel.py:8-28)."""
+    batch_size: int
+    context_len: int
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    kv_dtype: str
+    page_size: int
+
+    @property
+    def attention(self) -> str:
+        if self.num_q_heads == self.num_kv_heads:
+            return "MHA"
+        if self.num_kv_heads == 1:
+            return "MQA"
+        return "GQA"
+
+    @property
+    def kv_bytes(self) -> int:
+        dtype_bytes = 1 if self.kv_dtype == "fp8" else 2
+        return (self.batch_size * self.context_len * self.num_kv_heads * self.head_dim * 2
+                * dtype_bytes)
+
+
+class B2DDecodeKernel:
+    """Kernel(shape).run() adapter.  Lengths default to context_len for every
+    sequence with identity page order (the reference's inputs); seqlen_lo /
+    seqlen_hi / page_perm / seed select BASELINE-style distributions."""
+
+    def __init__(self, shape: DecodeShape, seqlen_lo: Optional[int] = None,
+                 seqlen_hi: Optional[int] = None, page_perm: bool = False, seed: int = 0,
+                 kv_scale_range=None, use_graph: bool = False):
+        if not torch.cuda.is_available():
+            raise RuntimeError("CUDA is required")
+        self.shape = shape
+        lo = seqlen_lo if seqlen_lo is not None else shape.context_len
+        hi = seqlen_hi if seqlen_hi is not None else shape.context_len
+        fp8 = shape.kv_dtype == "fp8"
+        self.workload = W.GqaWorkload(
+            "decodebench", shape.batch_size, shape.num_q_heads, shape.num_kv_heads,
+            shape.head_dim, shape.page_size, shape.kv_dtype, lo, hi,
+            q_dtype="fp16" if shape.kv_dtype == "fp16" else "bf16", seed=seed,
+            page_perm=page_perm, kv_scale_range=(kv_scale_range or ((1.0, 1.0) if fp8 else None)))
+        self.x = W.make_gqa_inputs(self.workload, torch.device("cuda"))
+        x = self.x
+        self.decoder = api.GqaDecoder(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"],
+                                      x["block_table"], x["softmax_scale"], k_scale=x["k_scale"],
+                                      v_scale=x["v_scale"])
+        self.use_graph = use_graph
+        if use_graph:
+            self.decoder.capture()
+
+    def run(self):
+        return self.decoder.replay() if self.use_graph else self.decoder.run()
+
+    @property
+    def algorithmic_bytes(self) -> int:
+        return W.gqa_algorithmic_bytes(self.workload, self.x["cache_seqlens"].cpu())
+
+    @property
+    def kv_bytes_exact(self) -> int:
+        return W.gqa_kv_bytes_reference(self.workload, self.x["cache_seqlens"].cpu())
+
+
+def cuda_time_ms(fn, repeat: int) -> list:
+    """One CUDA-event pair per call, synchronised (flashinfer_benchmark.py:17-27)."""
+    times = []
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    for _ in range(repeat):
+        start.record()
+        fn()
+        end.record()
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end))
+    return times
+
+
+def percentile(values, pct: float) -> float:
+    values = sorted(values)
+    if not values:
+        return float("nan")
+    index = min(len(values) - 1, max(0, math.ceil(pct / 100 * len(values)) - 1))
+    return values[index]
+
+
+def parse_args(argv=None) -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description="Benchmark the b2d paged decode kernel.")
+    ap.add_argument("--batch-size", type=int, required=True)
+    ap.add_argument("--context-len", type=int, required=True)
+    ap.add_argument("--num-q-heads", type=int, required=True)
+    ap.add_argument("--num-kv-heads", type=int, required=True)
+    ap.add_argument("--head-dim", type=int, required=True)
+    ap.add_argument("--kv-dtype", required=True, choices=["bf16", "fp16", "fp8"])
+    ap.add_argument("--page-size", type=int, required=True)
+    ap.add_argument("--warmup-steps", type=int, default=20)
+    ap.add_argument("--repeat", type=int, default=100)
+    ap.add_argument("--output", type=Path, required=True)
+    ap.add_argument("--seqlen-lo", type=int, default=None)
+    ap.add_argument("--seqlen-hi", type=int, default=None)
+    ap.add_argument("--page-perm", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cuda-graph", action="store_true")
+    return ap.parse_args(argv)
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    shape = DecodeShape(args.batch_size, args.context_len, args.num_q_heads, args.num_kv_heads,
+                        args.head_dim, args.kv_dtype, args.page_size)
+    kernel = B2DDecodeKernel(shape, args.seqlen_lo, args.seqlen_hi, args.page_perm, args.seed,
+                             use_graph=args.cuda_graph)
+    for _ in range(args.warmup_steps):
+        kernel.run()
+    torch.cuda.synchronize()
+    times_ms = cuda_time_ms(kernel.run, args.repeat)
+    avg_ms = sum(times_ms) / len(times_ms)
+    p50_ms = percentile(times_ms, 50)
+    p95_ms = percentile(times_ms, 95)
+    kv_bytes = kernel.kv_bytes_exact
+    alg = kernel.algorithmic_bytes
+    result = {
+        "run_id": os.environ.get("DECODEBENCH_RUN_ID"),
+        "timestamp": datetime.now(timezone.utc).isoformat(),
+        "gpu": torch.cuda.get_device_name(),
+        "backend": "b2d_decode",
+        "kernel_path": "b2d gqa_mma_kernel (sm_100a) via libb2d.so",
+        "layer": "kernel",
+        "workload_id": os.environ.get("DECODEBENCH_WORKLOAD_ID"),
+        "attention": shape.attention,
+        "kv_dtype": shape.kv_dtype,
+        "page_size": shape.page_size,
+        "batch_size": shape.batch_size,
+        "context_len": shape.context_len,
+        "decode_steps": 1,
+        "compare_latency_us": p50_ms * 1000.0,
+        "kernel_latency_avg_us": avg_ms * 1000.0,
+        "kernel_latency_p50_us": p50_ms * 1000.0,
+        "kernel_latency_p95_us": p95_ms * 1000.0,
+        "approx_kv_bytes_read": kv_bytes,
+        "approx_effective_kv_bandwidth_gb_s": kv_bytes / (p50_ms * 1e6),
+        "peak_allocated_gb": torch.cuda.max_memory_allocated() / 1e9,
+        "selected_backend": "b2d_decode",
+        "fallback": False,
+        "fallback_reason": None,
+        "notes": "Paged decode through b200decode.GqaDecoder.run (one C-ABI call per run).",
+        "roofline_bytes": alg,
+        "achieved_tb_s": alg / (p50_ms * 1e-3) / 1e12,
+        "seqlen_lo": kernel.workload.seqlen_lo,
+        "seqlen_hi": kernel.workload.seqlen_hi,
+        "seed": args.seed,
+        "page_perm": args.page_perm,
+        "cuda_graph": args.cuda_graph,
+    }
+    args.output.parent.mkdir(parents=True, exist_ok=True)
+    args.output.write_text(json.dumps(result, indent=2) + "\n", encoding="utf-8")
+    print(json.dumps(result))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -209,3 +209,19 @@ def test_decoder_plan_run_and_graph_replay(cuda):
     out, lse = dec.replay()
     torch.cuda.synchronize()
     assert_parity(out, lse, *oracle_gqa(x))
+
+
+def test_decodebench_adapter_writes_reference_schema(cuda, tmp_path):
+    import json
+    from b200decode import decodebench
+    out = tmp_path / "r.json"
+    rc = decodebench.main(["--batch-size", "8", "--context-len", "1000", "--num-q-heads", "32",
+                           "--num-kv-heads", "8", "--head-dim", "128", "--kv-dtype", "bf16",
+                           "--page-size", "16", "--warmup-steps", "2", "--repeat", "5",
+                           "--output", str(out), "--cuda-graph"])
+    assert rc == 0
+    d = json.loads(out.read_text())
+    for k in ("backend", "compare_latency_us", "kernel_latency_p50_us", "approx_kv_bytes_read",
+              "approx_effective_kv_bandwidth_gb_s", "fallback", "attention"):
+        assert k in d
+    assert d["backend"] == "b2d_decode" and d["approx_kv_bytes_read"] == 8 * 1000 * 8 * 128 * 4

@@ -94,3 +94,11 @@ def test_tp_head_gather_layout_gloo_world2():
         p.join(60)
     res = dict(q.get(timeout=10) for _ in range(2))
     assert res == {0: True, 1: True}
+
+
+def test_decodebench_shape_matches_reference_record():
+    from b200decode.decodebench import DecodeShape
+    s = DecodeShape(64, 4096, 32, 8, 128, "bf16", 16)
+    assert s.attention == "GQA" and s.kv_bytes == 64 * 4096 * 8 * 128 * 2 * 2
+    assert DecodeShape(1, 10, 8, 8, 64, "fp8", 16).kv_bytes == 10 * 8 * 64 * 2
+    assert DecodeShape(1, 10, 8, 1, 64, "fp16", 16).attention == "MQA"
