@@ -6,7 +6,7 @@
 
 namespace b2d {
 
-constexpr int kMlaMaxRows = 2048;   // sequences per launch (row table in shared memory)
+constexpr int kMlaMaxRows = 384;    // sequences per launch (row table in shared memory)
 
 struct MlaPlan {
   int nr;            // CTA pairs (ranges)

@@ -5,7 +5,7 @@
 // 576; V is the first 512 columns of the same cache row.
 //   S = q . K^T * scale,  out = softmax(S) . V,  lse = ln sum exp(S)
 //
-// Work: a CTA pair shares one range of 32-token chunks (the same balanced
+// Work: a CTA pair shares one range of 64-token chunks (the same balanced
 // stream-K cut over all sequences as the GQA kernel); CTA 2r+h computes the
 // 64 query heads [64h, 64h+64) of range r.  Both CTAs of a pair stream the
 // same KV tiles close together in time, so the second read is an L2 hit.
@@ -14,8 +14,8 @@
 // rows to 16 lanes of each 32-lane quadrant, lane half 0 (lanes 0-15,
 // 32-47, ...) or lane half 1 (16-31, ...) as the address selects.  The O
 // accumulator [64 heads x 512] takes columns 0-255 of both halves (half 0:
-// dims 0-255, half 1: dims 256-511); the score tiles S [64 heads x 32 tokens]
-// (double-buffered) take columns 256-319 of half 0.  Thread i of softmax
+// dims 0-255, half 1: dims 256-511); the score tiles S [64 heads x 64 tokens]
+// (double-buffered) take columns 256-383 of half 0.  Thread i of softmax
 // warp w owns head 16w + (i & 15): lanes < 16 read its S row (one whole row
 // per thread: row max and sum need no shuffles) and hold O dims 0-255, lanes
 // >= 16 hold O dims 256-511.  Rescaling O rewrites columns 0-255 only, so it
@@ -59,14 +59,14 @@ namespace mla {
 constexpr int kHeads = 64;         // query heads per CTA
 constexpr int kDqk = 576, kDv = 512;
 constexpr int kCB = kDqk / 64;     // 128-byte column blocks per row (9)
-constexpr int kT = 32;             // tokens per chunk
-constexpr int kStages = 3;
+constexpr int kT = 64;             // tokens per chunk (one TMA box; page size % 64 == 0)
+constexpr int kStages = 2;
 constexpr uint32_t kQBytes = kCB * kHeads * 128;     // 73728
-constexpr uint32_t kStageBytes = kCB * kT * 128;     // 36864
-constexpr uint32_t kPBytes = kHeads * 128;           // 8192 (32 tokens used of 64)
+constexpr uint32_t kStageBytes = kCB * kT * 128;     // 73728
 constexpr int kSplit = 1;          // independent QK accumulators per score tile
-constexpr int kSBuf = 2;           // score tiles in TMEM (lane half 0, columns 256 + 128k)
-constexpr int kPBuf = 3;           // P tiles in shared memory
+constexpr int kSBuf = 2;           // score tiles in TMEM (lane half 0, columns 256 + 64k)
+constexpr int kPBuf = 1;           // P tile in shared memory (64 heads x 64 tokens bf16)
+constexpr uint32_t kPBytes = kHeads * 128;           // 8192
 constexpr int kAhead = 1;          // QK tiles issued ahead of the oldest pending P.V
 constexpr float kLazy = 8.f;                         // lazy-rescale threshold, log2 units
 constexpr int kThreads = 6 * 32;
@@ -312,11 +312,11 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t pa = sbase + kOffP + (j % kPBuf) * kPBytes;
+          const uint32_t pa = sbase + kOffP + (uint32_t)((j % kPBuf) * kPBytes);
           const uint32_t vb = sbase + kOffKV + stage * kStageBytes;
-#pragma unroll
           const uint64_t pd0 = umma_desc_sw128(pa, 16, 1024);
           const uint64_t vd0 = umma_desc_sw128(vb, kT * 128, 1024);
+#pragma unroll
           for (int ks = 0; ks < kT / 16; ++ks) {
             const uint64_t ad = pd0 + (uint64_t)((ks * 32) >> 4);
 #pragma unroll
@@ -431,7 +431,9 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         if (!mla_wait(s_full + i % kSBuf, (uint32_t)((i / kSBuf) & 1), p.status)) { ok = false; break; }
         tc_fence_after();
         float sv[kT];
-        tmem_ld32(t_warp + 256u + (uint32_t)((i % kSBuf) * kSplit * kT), sv);
+#pragma unroll
+        for (int c = 0; c < kT; c += 32)
+          tmem_ld32(t_warp + 256u + (uint32_t)((i % kSBuf) * kSplit * kT + c), sv + c);
 #pragma unroll
         for (int part = 1; part < kSplit; ++part) {
           float sp[kT];
@@ -470,12 +472,14 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           }
           tc_fence_before();
         }
-        // P row (bf16) into the swizzled K-major P buffer; P(i-2) must be consumed.
+        // P(i - kPBuf) must be consumed before its TMEM buffer is rewritten.
         if (i >= kPBuf) {
           if (!mla_wait(pv_done + i % kPBuf, (uint32_t)(((i - kPBuf) / kPBuf) & 1), p.status)) { ok = false; break; }
         }
-        uint8_t* pbuf = smem + kOffP + (i % kPBuf) * kPBytes;
         if (s_lane) {
+          // P row (bf16) into the swizzled K-major P tile: row hr is 128-byte
+          // line hr, its 16-byte chunk c (8 tokens) sits at c ^ (hr & 7).
+          uint8_t* pbuf = smem + kOffP + (i % kPBuf) * kPBytes;
           float psum = 0.f;
           uint32_t pk[kT / 2];
 #pragma unroll
@@ -485,7 +489,6 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
             pk[t / 2] = pack2<true>(p0, p1);
           }
           l += psum;
-          // row hr: 128-byte line hr; 16-byte chunk c (8 tokens) at c ^ (hr & 7)
 #pragma unroll
           for (int c = 0; c < kT / 8; ++c) {
             const uint32_t a = smem_u32(pbuf) + hr * 128 + (((c ^ (hr & 7)) & 7) << 4);
