@@ -176,6 +176,40 @@ int b2d_mla_workspace_bytes(const b2d_mla_args* args, size_t* bytes);
 int b2d_decode_mla(const b2d_mla_args* args, void* stream);
 
 /*
+ * KV-cache append (the write side of the paged cache that the decode reads):
+ * token t's key/value rows go to slot slot_mapping[t] = page * page_size +
+ * offset, optionally quantised to FP8-e4m3 as round-to-nearest-even of
+ * x / scale[kv_head], saturated to +-448.  Replaces
+ * decodebench/vllm_paged_kernel.py:160-172 ops.reshape_and_cache(key, value,
+ * key_cache, value_cache, slot_mapping, kv_cache_dtype, k_scale, v_scale)
+ * for the NHD / HND page layouts (strides as in b2d_gqa_args).
+ *   key, value   [num_tokens, num_kv_heads, head_dim] (bf16 | fp16)
+ *   slot_mapping int64 [num_tokens]; a negative slot skips the token
+ *   caches       in the source type, or FP8_E4M3 with k_scale / v_scale
+ *   bad_slots    optional int counter (device), incremented for every
+ *                slot >= num_pages * page_size (such tokens are skipped)
+ */
+typedef struct b2d_append_args {
+  const void* key;
+  const void* value;
+  int64_t src_stride_t, src_stride_h;
+  void* k_cache;
+  void* v_cache;
+  int64_t k_stride_page, k_stride_tok, k_stride_head;
+  int64_t v_stride_page, v_stride_tok, v_stride_head;
+  int64_t num_pages;
+  const int64_t* slot_mapping;
+  const float* k_scale;
+  const float* v_scale;
+  int* bad_slots;
+  int32_t num_tokens, num_kv_heads, head_dim, page_size;
+  int32_t src_dtype, cache_dtype;
+  int32_t reserved[2];
+} b2d_append_args;
+
+int b2d_append_kv(const b2d_append_args* args, void* stream);
+
+/*
  * Reads (and clears, when clear != 0) the device status word that kernels
  * set when an in-kernel wait ran out of time or a page id was out of range.
  * Synchronises `stream`.  Returns 0 or the matching negative b2d_status.

@@ -203,3 +203,34 @@ def merge_partials(m, l, o):
     den = (l * w).sum(axis=1)
     num = (o * w[:, :, None]).sum(axis=1)
     return num / den[:, None], big + np.log(den)
+
+
+# ---------------------------------------------------------------------------
+# KV-cache append (vllm_paged_kernel.py:160-172, reshape_and_cache)
+# ---------------------------------------------------------------------------
+
+
+def append_kv(cache, rows, slots, page_size, scale=None, fp8=False):
+    """Reference for b2d_append_kv on one cache (numpy, in place).
+
+    cache: [num_pages, P, H, D] array of stored values (uint8 e4m3 codes when
+    fp8, else float); rows: [T, H, D] float32 source values; slots: [T] int
+    (negative = skip, >= num_pages * P = skip and counted).  FP8 stores
+    e4m3(x * (1 / scale)) computed in float32, round-to-nearest-even,
+    saturated.  Returns the number of out-of-range slots."""
+    cap = cache.shape[0] * page_size
+    bad = 0
+    for t, slot in enumerate(np.asarray(slots).tolist()):
+        if slot < 0:
+            continue
+        if slot >= cap:
+            bad += 1
+            continue
+        page, off = divmod(slot, page_size)
+        x = np.asarray(rows[t], dtype=np.float32)
+        if fp8:
+            inv = (np.float32(1.0) / np.asarray(scale, dtype=np.float32))[:, None]
+            cache[page, off] = f64_to_e4m3_bits((x * inv).astype(np.float32).astype(np.float64))
+        else:
+            cache[page, off] = x
+    return bad

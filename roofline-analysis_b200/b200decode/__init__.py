@@ -13,6 +13,7 @@ library or without a CUDA device raises.
 """
 from .api import (  # noqa: F401
     B2DError,
+    append_kv,
     DecodeWorkspace,
     GqaDecoder,
     check_device_status,

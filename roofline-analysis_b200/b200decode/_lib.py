@@ -20,6 +20,7 @@ EXPORTED = (
     "b2d_mla_workspace_bytes",
     "b2d_decode_mla",
     "b2d_check_device_status",
+    "b2d_append_kv",
     "b2d_gqa_plan",
     "b2d_error_string",
     "b2d_version",
@@ -64,6 +65,21 @@ class MlaArgs(C.Structure):
     ]
 
 
+class AppendArgs(C.Structure):
+    _fields_ = [
+        ("key", C.c_void_p), ("value", C.c_void_p),
+        ("src_stride_t", C.c_int64), ("src_stride_h", C.c_int64),
+        ("k_cache", C.c_void_p), ("v_cache", C.c_void_p),
+        ("k_stride_page", C.c_int64), ("k_stride_tok", C.c_int64), ("k_stride_head", C.c_int64),
+        ("v_stride_page", C.c_int64), ("v_stride_tok", C.c_int64), ("v_stride_head", C.c_int64),
+        ("num_pages", C.c_int64), ("slot_mapping", C.c_void_p),
+        ("k_scale", C.c_void_p), ("v_scale", C.c_void_p), ("bad_slots", C.c_void_p),
+        ("num_tokens", C.c_int32), ("num_kv_heads", C.c_int32), ("head_dim", C.c_int32),
+        ("page_size", C.c_int32), ("src_dtype", C.c_int32), ("cache_dtype", C.c_int32),
+        ("reserved", C.c_int32 * 2),
+    ]
+
+
 _lib = None
 
 
@@ -83,6 +99,7 @@ def load() -> C.CDLL:
     lib.b2d_decode_gqa_static_scratch.argtypes = [C.POINTER(GqaArgs), C.c_void_p]
     lib.b2d_mla_workspace_bytes.argtypes = [C.POINTER(MlaArgs), C.POINTER(C.c_size_t)]
     lib.b2d_decode_mla.argtypes = [C.POINTER(MlaArgs), C.c_void_p]
+    lib.b2d_append_kv.argtypes = [C.POINTER(AppendArgs), C.c_void_p]
     lib.b2d_check_device_status.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
     lib.b2d_gqa_plan.argtypes = [C.POINTER(GqaArgs), C.POINTER(C.c_int32), C.POINTER(C.c_int32),
                                  C.POINTER(C.c_int32)]

@@ -306,6 +306,52 @@ def decode_mla(q: torch.Tensor, kv_cache: torch.Tensor, cache_seqlens: torch.Ten
     return out, lse
 
 
+def append_kv(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+              slot_mapping: torch.Tensor, *, k_scale: Optional[torch.Tensor] = None,
+              v_scale: Optional[torch.Tensor] = None, kv_layout: str = "NHD",
+              bad_slots: Optional[torch.Tensor] = None) -> None:
+    """Write new tokens' K/V rows into the paged caches (vLLM's
+    reshape_and_cache, decodebench/vllm_paged_kernel.py:160-172).
+
+    key, value: [T, Hkv, D] bf16/fp16; slot_mapping: int64 [T] with slot =
+    page * P + offset (negative = skip).  Caches in the source dtype, or
+    float8_e4m3fn: stored value = e4m3(x / scale[head]) (round-to-nearest-even,
+    saturated).  bad_slots: optional int32 [1] counter of out-of-range slots."""
+    if not key.is_cuda:
+        raise RuntimeError("append_kv needs CUDA tensors (there is no CPU path)")
+    lib = _lib.load()
+    if key.shape != value.shape or key.dim() != 3 or key.dtype != value.dtype:
+        raise ValueError("key and value must be matching [T, Hkv, D] tensors")
+    if key.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("key/value must be bf16 or fp16")
+    if key.stride(-1) != 1 or value.stride() != key.stride():
+        raise ValueError("key and value need the same strides and a contiguous head_dim")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (key.shape[0],):
+        raise ValueError("slot_mapping must be int64 [T]")
+    if k_cache.dtype != v_cache.dtype or k_cache.dtype not in (key.dtype, torch.float8_e4m3fn):
+        raise ValueError("caches must be in the source dtype or float8_e4m3fn")
+    ks_p, ks_t, ks_h, page, hkv = _layout_strides(k_cache, kv_layout)
+    vs_p, vs_t, vs_h, _, _ = _layout_strides(v_cache, kv_layout)
+    if hkv != key.shape[1] or k_cache.shape[-1] != key.shape[2]:
+        raise ValueError("cache heads / head_dim do not match key")
+    a = _lib.AppendArgs()
+    a.key, a.value = key.data_ptr(), value.data_ptr()
+    a.src_stride_t, a.src_stride_h = key.stride(0), key.stride(1)
+    a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    a.k_stride_page, a.k_stride_tok, a.k_stride_head = ks_p, ks_t, ks_h
+    a.v_stride_page, a.v_stride_tok, a.v_stride_head = vs_p, vs_t, vs_h
+    a.num_pages = k_cache.shape[0]
+    a.slot_mapping = slot_mapping.data_ptr()
+    fp8 = k_cache.dtype == torch.float8_e4m3fn
+    a.k_scale = _ptr(k_scale) if fp8 else None
+    a.v_scale = _ptr(v_scale) if fp8 else None
+    a.bad_slots = _ptr(bad_slots)
+    a.num_tokens, a.num_kv_heads, a.head_dim, a.page_size = key.shape[0], hkv, key.shape[2], page
+    a.src_dtype, a.cache_dtype = _DT[key.dtype], _DT[k_cache.dtype]
+    stream = torch.cuda.current_stream(key.device).cuda_stream
+    _check(lib.b2d_append_kv(C.byref(a), C.c_void_p(stream)), "b2d_append_kv")
+
+
 def check_device_status(workspace: Optional[DecodeWorkspace] = None, device=None,
                         clear: bool = True) -> None:
     """Synchronise and raise B2DError if a kernel recorded a timeout or an

@@ -118,3 +118,19 @@ def test_fp8_workload_dequantises_to_unit_scale_values():
     k = to_oracle(x["k_cache"]) * x["k_scale"].double().numpy()[None, None, :, None]
     assert 0.9 < k.std() < 1.1
     assert float(x["k_scale"].min()) >= 0.01 and float(x["k_scale"].max()) <= 0.1
+
+
+def test_append_oracle_quantises_like_torch_and_skips_slots():
+    rng = np.random.default_rng(3)
+    cache = np.zeros((4, 16, 2, 64), dtype=np.uint8)
+    rows = rng.normal(size=(5, 2, 64)).astype(np.float32) * 3
+    scale = np.array([0.05, 0.2], dtype=np.float32)
+    slots = np.array([0, 17, -1, 63, 64])
+    bad = R.append_kv(cache, rows, slots, 16, scale, fp8=True)
+    assert bad == 1
+    want = (torch.from_numpy(rows) * (1 / torch.from_numpy(scale))[None, :, None]).to(
+        torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(cache[0, 0], want[0])
+    np.testing.assert_array_equal(cache[1, 1], want[1])
+    np.testing.assert_array_equal(cache[3, 15], want[3])
+    assert not cache[0, 2].any()   # slot 2 untouched by the skipped token
