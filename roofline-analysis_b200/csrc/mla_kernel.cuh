@@ -69,6 +69,10 @@ constexpr int kPBuf = 1;           // P tile in shared memory (64 heads x 64 tok
 constexpr uint32_t kPBytes = kHeads * 128;           // 8192
 constexpr int kAhead = 1;          // QK tiles issued ahead of the oldest pending P.V
 constexpr float kLazy = 8.f;                         // lazy-rescale threshold, log2 units
+#ifndef B2D_MLA_L2_AHEAD
+#define B2D_MLA_L2_AHEAD 2
+#endif
+constexpr int kL2Ahead = B2D_MLA_L2_AHEAD;           // chunks prefetched into L2 past the ring
 constexpr int kThreads = 6 * 32;
 // shared-memory map (offsets from the 1024-aligned base)
 constexpr uint32_t kOffQ = 0;
@@ -80,6 +84,30 @@ constexpr uint32_t kNumBars = 2 * kStages + 2 + kSBuf + kPBuf + kPBuf + 2;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffRows = kOffTmem + 16;
 }  // namespace mla
+
+#ifndef B2D_MLA_EVICT_FIRST
+#define B2D_MLA_EVICT_FIRST 0
+#endif
+// Cache policy of the KV loads: the head-pair partner CTA reads each tile
+// again shortly after, so by default it stays in L2 normally.
+__device__ __forceinline__ uint64_t kv_policy() {
+  uint64_t p;
+  if (B2D_MLA_EVICT_FIRST)
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  else
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// L2 prefetch of one 5-D TMA box (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_5d(const CUtensorMap* map, int c1, int c2, int c3,
+                                                int c4) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
                                                     uint32_t sbo_bytes) {
@@ -264,7 +292,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
   if (warp == 4) {
     // ---------------- TMA producer ----------------
     if (lane == 0 && active) {
-      const uint64_t policy = policy_evict_first();
+      const uint64_t policy = kv_policy();
       int row = find_row(row_start, R, x0);
       int cur = -1, nq = 0, s = 0;
       uint32_t ph = 0;
@@ -283,6 +311,19 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         if (pg < 0 || pg >= p.num_pages) {
           record_status(p.status, kStatusBounds);
           pg = 0;
+        }
+        // Warm L2 for the chunks after the ones the stage ring can hold, so
+        // their loads (and the head-pair partner's) come from L2.
+#pragma unroll
+        for (int d = kStages; d < kStages + kL2Ahead; ++d) {
+          const int xa = x + d;
+          if (xa >= x1) break;
+          int ra = row;
+          while (xa >= row_start[ra + 1]) ++ra;
+          const int ta = (xa - row_start[ra]) * kT;
+          const int pa = ta / p.P;
+          const int pga = __ldg(p.block_table + (int64_t)ra * p.bt_stride + pa);
+          if (pga >= 0 && pga < p.num_pages) tma_prefetch_5d(&tmap_kv, ta - pa * p.P, 0, pga, 0);
         }
         if (!mla_wait(kv_empty + s, ph ^ 1u, p.status)) break;
         mbar_arrive_expect_tx(kv_full + s, kStageBytes);
