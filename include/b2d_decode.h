@@ -88,6 +88,9 @@ enum b2d_dtype {
  *            num_q_heads] fp32 (may be NULL).
  * Query head h reads KV head h / (num_q_heads / num_kv_heads).
  * A sequence of length 0 yields out = 0 and lse = -inf.
+ * Built: head_dim 64, 128 and 256 (any page size, all cache types) and 192
+ * (bf16/fp16 caches with page_size % 16 == 0); group (num_q_heads /
+ * num_kv_heads) <= 32.  Other combinations return B2D_ERR_UNSUPPORTED.
  */
 typedef struct b2d_gqa_args {
   const void* q;

@@ -50,7 +50,8 @@ static int validate(const b2d_gqa_args* a, bool need_pointers) {
       a->max_pages_per_seq <= 0)
     return B2D_ERR_INVALID_ARG;
   if (a->num_q_heads % a->num_kv_heads != 0) return B2D_ERR_INVALID_ARG;
-  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return B2D_ERR_UNSUPPORTED;
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 192 && a->head_dim != 256)
+    return B2D_ERR_UNSUPPORTED;
   if (a->q_dtype != B2D_BF16 && a->q_dtype != B2D_FP16) return B2D_ERR_UNSUPPORTED;
   if (a->kv_dtype != a->q_dtype && a->kv_dtype != B2D_FP8_E4M3) return B2D_ERR_UNSUPPORTED;
   const int group = a->num_q_heads / a->num_kv_heads;
@@ -85,11 +86,14 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
   // fp8 tiles use whole 128-byte lines per head row, so head_dim >= 128.
   pl->mma = use_mma && (a->page_size % 16 == 0) &&
             !(a->kv_dtype == B2D_FP8_E4M3 && a->head_dim < 128);
+  // head_dim 192 is built for the tensor-core path with 16-bit caches only
+  // (fp8 tiles need whole 128-byte lines per head row: head_dim % 128 == 0).
+  if (a->head_dim == 192 && (!pl->mma || a->kv_dtype == B2D_FP8_E4M3)) return B2D_ERR_UNSUPPORTED;
   if (pl->mma) {
     // Tensor-core consumer: a warp takes GW <= 16 query heads (<= 8 at
-    // head_dim 256, to bound the accumulator registers) of one KV head; a
+    // head_dim 192 and 256, to bound the accumulator registers) of one KV head; a
     // chunk is 16 tokens of HK KV heads.
-    const int gw_cap = a->head_dim == 256 ? 8 : 16;
+    const int gw_cap = a->head_dim >= 192 ? 8 : 16;
     int wph = 1;
     while (group % wph != 0 || group / wph > gw_cap) ++wph;
     pl->wph = wph;
@@ -192,7 +196,7 @@ template <int D, int KIND, typename QT>
 static int launch_mma(const GqaPlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
                       const GqaParams& p, cudaStream_t st, int flags) {
   if (pl.np == 2) {
-    if constexpr (D == 256) return B2D_ERR_UNSUPPORTED;
+    if constexpr (D >= 192) return B2D_ERR_UNSUPPORTED;
     else
       return launch_k(gqa_mma_kernel<D, KIND, QT, 2>, gqa_combine_kernel<D, QT>, pl, tk, tv, p,
                       st, flags);
@@ -216,19 +220,25 @@ static int launch_d(const b2d_gqa_args* a, const GqaPlan& pl, const CUtensorMap&
                     const CUtensorMap& tv, const GqaParams& p, cudaStream_t st) {
   const int flags = a->flags;
   const bool qbf = a->q_dtype == B2D_BF16;
-  if (pl.mma) {
-    if (a->kv_dtype == B2D_FP8_E4M3)
-      return qbf ? launch_mma<D, kKvFp8, __nv_bfloat16>(pl, tk, tv, p, st, flags)
-                 : launch_mma<D, kKvFp8, __half>(pl, tk, tv, p, st, flags);
+  if constexpr (D == 192) {
+    // the plan admits only the tensor-core path with 16-bit caches here
     return qbf ? launch_mma<D, kKvBf16, __nv_bfloat16>(pl, tk, tv, p, st, flags)
                : launch_mma<D, kKvFp16, __half>(pl, tk, tv, p, st, flags);
+  } else {
+    if (pl.mma) {
+      if (a->kv_dtype == B2D_FP8_E4M3)
+        return qbf ? launch_mma<D, kKvFp8, __nv_bfloat16>(pl, tk, tv, p, st, flags)
+                   : launch_mma<D, kKvFp8, __half>(pl, tk, tv, p, st, flags);
+      return qbf ? launch_mma<D, kKvBf16, __nv_bfloat16>(pl, tk, tv, p, st, flags)
+                 : launch_mma<D, kKvFp16, __half>(pl, tk, tv, p, st, flags);
+    }
+    if (a->kv_dtype == B2D_FP8_E4M3) {
+      return qbf ? launch_hqw<D, kKvFp8, __nv_bfloat16>(pl, tk, tv, p, st, flags)
+                 : launch_hqw<D, kKvFp8, __half>(pl, tk, tv, p, st, flags);
+    }
+    return qbf ? launch_hqw<D, kKvBf16, __nv_bfloat16>(pl, tk, tv, p, st, flags)
+               : launch_hqw<D, kKvFp16, __half>(pl, tk, tv, p, st, flags);
   }
-  if (a->kv_dtype == B2D_FP8_E4M3) {
-    return qbf ? launch_hqw<D, kKvFp8, __nv_bfloat16>(pl, tk, tv, p, st, flags)
-               : launch_hqw<D, kKvFp8, __half>(pl, tk, tv, p, st, flags);
-  }
-  return qbf ? launch_hqw<D, kKvBf16, __nv_bfloat16>(pl, tk, tv, p, st, flags)
-             : launch_hqw<D, kKvFp16, __half>(pl, tk, tv, p, st, flags);
 }
 
 static int encode_kv_map(CUtensorMap* map, const void* base, const b2d_gqa_args* a,
@@ -338,6 +348,7 @@ extern "C" int b2d_decode_gqa(const b2d_gqa_args* a, void* stream) {
     switch (a->head_dim) {
       case 64: rc = launch_d<64>(a, pl, tk, tv, p, st); break;
       case 128: rc = launch_d<128>(a, pl, tk, tv, p, st); break;
+      case 192: rc = launch_d<192>(a, pl, tk, tv, p, st); break;
       default: rc = launch_d<256>(a, pl, tk, tv, p, st); break;
     }
     if (rc) return rc;

@@ -72,6 +72,8 @@ def test_workspace_query_and_plan_on_host():
 
 @pytest.mark.parametrize("kw,code", [
     (dict(head_dim=96), -2),                 # unsupported head_dim
+    (dict(head_dim=192, kv_dtype=_lib.B2D_FP8_E4M3), -2),  # fp8 needs head_dim % 128 == 0
+    (dict(head_dim=192, page_size=8), -2),   # 192 only on the tensor-core path (page % 16)
     (dict(num_q_heads=30), -1),              # not a multiple of num_kv_heads
     (dict(q_dtype=_lib.B2D_FP8_E4M3), -2),   # q must be 16-bit
     (dict(kv_dtype=_lib.B2D_FP16), -2),      # cache must match q or be fp8
@@ -82,6 +84,15 @@ def test_host_validation_rejects(kw, code):
     lib = _lib.load()
     n = C.c_size_t(0)
     assert lib.b2d_gqa_workspace_bytes(C.byref(_args(**kw)), C.byref(n)) == code
+
+
+def test_head_dim_192_is_planned_for_16bit_caches():
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    for page in (16, 64):
+        assert lib.b2d_gqa_workspace_bytes(C.byref(_args(head_dim=192, page_size=page)),
+                                           C.byref(n)) == 0
+        assert n.value > 0
 
 
 def test_decode_rejects_null_pointers_before_touching_a_gpu():

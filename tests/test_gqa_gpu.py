@@ -47,6 +47,39 @@ def test_head_dims_and_dtypes(cuda, d, dt):
     assert_parity(out, lse, *oracle_gqa(x))
 
 
+@pytest.mark.parametrize("dt", ["bf16", "fp16"])
+@pytest.mark.parametrize("hq,hkv,page", [(8, 2, 16), (32, 2, 64), (16, 16, 32)])
+def test_head_dim_192(cuda, dt, hq, hkv, page):
+    """head_dim 192 (tensor-core path, 16-bit caches)."""
+    w = SMALL.scaled(head_dim=192, kv_dtype=dt, q_dtype=dt, num_q_heads=hq, num_kv_heads=hkv,
+                     page_size=page)
+    x = _inputs(cuda, w, lens=[1, page + 3, 5 * page, 300, 0])
+    out, lse = _run(x)
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+@pytest.mark.parametrize("kw", [dict(kv_dtype="fp8", kv_scale_range=(0.01, 0.1)),
+                                dict(page_size=8)])
+def test_head_dim_192_unsupported_combinations(cuda, kw):
+    """fp8 at head_dim 192, or a page size that is not a multiple of 16,
+    is refused with B2D_ERR_UNSUPPORTED rather than computed wrongly."""
+    x = _inputs(cuda, SMALL.scaled(head_dim=192, **kw))
+    with pytest.raises(b200decode.B2DError, match="(?i)unsupported"):
+        _run(x)
+
+
+# Extended sweep (decodebench matrix_b200_extended.py:28-40 and
+# matrix_b200.py:214-228 shapes, at test sizes): GQA ratios 2-16, MQA
+# (group 32), head_dim 64 and 128, page 128.
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("hq,hkv", [(16, 8), (32, 8), (32, 4), (32, 2), (32, 1)])
+def test_extended_sweep_page128(cuda, d, hq, hkv):
+    w = SMALL.scaled(head_dim=d, num_q_heads=hq, num_kv_heads=hkv, page_size=128)
+    x = _inputs(cuda, w, lens=[1, 127, 128, 129, 700])
+    out, lse = _run(x)
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
 @pytest.mark.parametrize("page", [1, 4, 8, 16, 32, 64, 128, 48])
 def test_page_sizes(cuda, page):
     w = SMALL.scaled(page_size=page)
