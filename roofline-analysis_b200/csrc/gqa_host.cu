@@ -157,7 +157,7 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
 }
 
 template <typename Kern>
-static int launch_k(Kern kern, void (*combine)(const GqaParams, int), const GqaPlan& pl,
+static int launch_k(Kern kern, void (*combine)(const GqaParams, int, int), const GqaPlan& pl,
                     const CUtensorMap& tk, const CUtensorMap& tv, const GqaParams& p,
                     cudaStream_t st, int flags) {
   const int threads = 32 * (pl.nw + 1);
@@ -176,10 +176,11 @@ static int launch_k(Kern kern, void (*combine)(const GqaParams, int), const GqaP
     if (cudaGetLastError() != cudaSuccess) return B2D_ERR_CUDA;
   }
   const int R = p.B * p.HG;
-  const int64_t warps = (int64_t)R * pl.hk * pl.group;
-  const int blocks = (int)((warps * 32 + 255) / 256);
+  const int64_t merges = (int64_t)R * pl.hk * pl.group;
+  const int wpp = combine_warps_per_merge(merges);
+  const int blocks = (int)((merges + 8 / wpp - 1) / (8 / wpp));
   if (blocks > 0 && !(flags & B2D_FLAG_SKIP_COMBINE)) {
-    combine<<<blocks, 256, 0, st>>>(p, ctas);
+    combine<<<blocks, 256, 0, st>>>(p, ctas, wpp);
     if (cudaGetLastError() != cudaSuccess) return B2D_ERR_CUDA;
   }
   return B2D_OK;

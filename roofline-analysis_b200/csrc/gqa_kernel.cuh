@@ -533,53 +533,103 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
 
 // Merge the split partials of every row that more than one CTA touched
 // (cluster_decode_reduce.py:67-91 in log2 units), and write out = 0,
-// lse = -inf for rows of zero length.  One warp per (row, query head).
+// lse = -inf for rows of zero length.  `wpp` warps (1, 2, 4 or 8) merge one
+// (row, query head): with few rows (small batches) each row is split over
+// many CTAs and one warp per merge would leave most SMs idle.
 template <int D, typename QT>
-__global__ void __launch_bounds__(256) gqa_combine_kernel(const GqaParams p, int G) {
+__global__ void __launch_bounds__(256) gqa_combine_kernel(const GqaParams p, int G, int wpp) {
   constexpr float kLn2 = 0.69314718055994530942f;
   constexpr int EPL = D / 32;  // elements per lane
+  static_assert(EPL % 2 == 0, "combine loads float2 pairs");
+  // U segments per step, all loads issued before any is used (a chain of
+  // dependent L2 round trips otherwise).
+  constexpr int U = D >= 512 ? 2 : (D >= 256 ? 4 : 8);
+  __shared__ float red_acc[8][EPL][32];
+  __shared__ float red_w[8];
   const int R = p.B * p.HG;
   const int HQC = p.HK * p.group;
-  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (gw >= (int64_t)R * HQC) return;
-  const int row = (int)(gw / HQC);
-  const int qh_row = (int)(gw - (int64_t)row * HQC);
-  const int b = row / p.HG, hg = row - b * p.HG;
-  const int qh = hg * HQC + qh_row;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = warp % wpp;
+  const int64_t gw = (int64_t)blockIdx.x * (8 / wpp) + warp / wpp;
   const int64_t W = p.row_start_g[R];
   if (W < (int64_t)G) G = (int)W;  // the decode kernel's effective CTA count
-  const int rs = p.row_start_g[row], re = p.row_start_g[row + 1];
+  int mode = 0;                    // 0: nothing, 1: zero-length row, 2: merge
+  int row = 0, b = 0, qh = 0, qh_row = 0, nseg = 0;
+  int64_t seg0 = 0;
+  if (gw < (int64_t)R * HQC) {
+    row = (int)(gw / HQC);
+    qh_row = (int)(gw - (int64_t)row * HQC);
+    b = row / p.HG;
+    const int hg = row - b * p.HG;
+    qh = hg * HQC + qh_row;
+    const int rs = p.row_start_g[row], re = p.row_start_g[row + 1];
+    if (re == rs) {
+      mode = 1;
+    } else {
+      const int cf = cta_of_chunk(rs, W, G), cl = cta_of_chunk(re - 1, W, G);
+      if (cf != cl) {  // else written directly by the decode kernel
+        mode = 2;
+        nseg = cl - cf + 1;
+        seg0 = (int64_t)row + cf;
+      }
+    }
+  }
   QT* dst = reinterpret_cast<QT*>(p.out) + (int64_t)b * p.o_sb + (int64_t)qh * p.o_sh + lane * EPL;
-  if (re == rs) {
+  if (mode == 1 && sub == 0) {
 #pragma unroll
     for (int e = 0; e < EPL; ++e) dst[e] = QT(0.f);
     if (p.lse != nullptr && lane == 0) p.lse[(int64_t)b * p.lse_sb + qh] = -INFINITY;
-    return;
   }
-  const int cf = cta_of_chunk(rs, W, G), cl = cta_of_chunk(re - 1, W, G);
-  if (cf == cl) return;  // written directly by the decode kernel
-  const int nseg = cl - cf + 1;
-  const int64_t seg0 = (int64_t)row + cf;
-  float mx = -INFINITY;
-  for (int j = lane; j < nseg; j += 32) mx = fmaxf(mx, p.part_lse[(seg0 + j) * HQC + qh_row]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float acc[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-  float wsum = 0.f;
-  for (int j = 0; j < nseg; ++j) {
-    const float w = fast_exp2(p.part_lse[(seg0 + j) * HQC + qh_row] - mx);
-    wsum += w;
-    const float* src = p.part_o + ((seg0 + j) * HQC + qh_row) * D + lane * EPL;
+  float wsum = 0.f, mx = -INFINITY;
+  if (mode == 2) {
+    for (int j = lane; j < nseg; j += 32) mx = fmaxf(mx, p.part_lse[(seg0 + j) * HQC + qh_row]);
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[e] += w * src[e];
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int j0 = sub * U; j0 < nseg; j0 += wpp * U) {
+      float lv[U];
+      float2 v[U][EPL / 2];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + u < nseg ? j0 + u : nseg - 1;
+        lv[u] = p.part_lse[(seg0 + j) * HQC + qh_row];
+        const float* src = p.part_o + ((seg0 + j) * HQC + qh_row) * D + lane * EPL;
+#pragma unroll
+        for (int e = 0; e < EPL / 2; ++e) v[u][e] = *reinterpret_cast<const float2*>(src + 2 * e);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float w = (j0 + u < nseg) ? fast_exp2(lv[u] - mx) : 0.f;
+        wsum += w;
+#pragma unroll
+        for (int e = 0; e < EPL / 2; ++e) {
+          acc[2 * e] += w * v[u][e].x;
+          acc[2 * e + 1] += w * v[u][e].y;
+        }
+      }
+    }
   }
-  const float inv = 1.f / wsum;
+  if (wpp > 1) {
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) dst[e] = QT(acc[e] * inv);
-  if (p.lse != nullptr && lane == 0) p.lse[(int64_t)b * p.lse_sb + qh] = (mx + fast_log2(wsum)) * kLn2;
+    for (int e = 0; e < EPL; ++e) red_acc[warp][e][lane] = acc[e];
+    if (lane == 0) red_w[warp] = wsum;
+    __syncthreads();
+    if (mode == 2 && sub == 0) {
+      for (int w = 1; w < wpp; ++w) {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] += red_acc[warp + w][e][lane];
+        wsum += red_w[warp + w];
+      }
+    }
+  }
+  if (mode == 2 && sub == 0) {
+    const float inv = 1.f / wsum;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = QT(acc[e] * inv);
+    if (p.lse != nullptr && lane == 0) p.lse[(int64_t)b * p.lse_sb + qh] = (mx + fast_log2(wsum)) * kLn2;
+  }
 }
 
 }  // namespace b2d

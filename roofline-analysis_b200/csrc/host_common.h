@@ -29,4 +29,10 @@ int encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, cons
                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                      CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
+// Warps that merge one (row, query head) in the combine kernel: up to 8
+// when there are few merges, so small batches still fill the GPU.
+inline int combine_warps_per_merge(int64_t merges) {
+  return merges <= 256 ? 8 : merges <= 512 ? 4 : merges <= 1024 ? 2 : 1;
+}
+
 }  // namespace b2d

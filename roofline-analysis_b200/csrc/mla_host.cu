@@ -151,8 +151,10 @@ extern "C" int b2d_decode_mla(const b2d_mla_args* a, void* stream) {
       cp.HG = 1;
       cp.HK = 1;
       cp.group = 128;
-      const int blocks = (nb * 128 * 32 + 255) / 256;
-      gqa_combine_kernel<512, __nv_bfloat16><<<blocks, 256, 0, st>>>(cp, pl.nr);
+      const int64_t merges = (int64_t)nb * 128;
+      const int wpp = combine_warps_per_merge(merges);
+      const int blocks = (int)((merges + 8 / wpp - 1) / (8 / wpp));
+      gqa_combine_kernel<512, __nv_bfloat16><<<blocks, 256, 0, st>>>(cp, pl.nr, wpp);
       if (cudaGetLastError() != cudaSuccess) return B2D_ERR_CUDA;
     }
   }
