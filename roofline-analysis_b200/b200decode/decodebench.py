@@ -1,6 +1,8 @@
 """decodebench backend "b2d_decode": the adapter pair the reference's harness
 expects (decodebench/<x>_kernel.py + <x>_benchmark.py), for this library.
 
+GQA/MHA/MQA:
+
 Kernel side mirrors decodebench/flashinfer_kernel.py:41-116: the constructor
 builds q, the paged caches, the lengths and the block table for a shape (the
 reference's DecodeShape fields, decodebench/flashinfer_kernel.py:8-28), and
@@ -12,6 +14,12 @@ fields (lengths distribution, seed, roofline figures).
     python -m b200decode.decodebench --batch-size 64 --context-len 4096 \\
         --num-q-heads 32 --num-kv-heads 8 --head-dim 128 --kv-dtype bf16 \\
         --page-size 16 --output result.json [--seqlen-lo 1024 --seqlen-hi 8192]
+
+Absorbed MLA (mirrors decodebench/trtllm_mla_kernel.py:7-25 and
+trtllm_mla_benchmark.py:13-94; same shape fields, same record):
+
+    python -m b200decode.decodebench mla --batch-size 32 --context-len 32768 \\
+        --num-q-heads 128 --kv-dtype bf16 --page-size 64 --output result.json
 """
 from __future__ import annotations
 
@@ -96,6 +104,70 @@ class B2DDecodeKernel:
         return W.gqa_kv_bytes_reference(self.workload, self.x["cache_seqlens"].cpu())
 
 
+@dataclasses.dataclass(frozen=True)
+class MlaDecodeShape:
+    """Field-for-field the reference's TRTLLMMLADecodeShape
+    (decodebench/trtllm_mla_kernel.py:7-25)."""
+    batch_size: int
+    context_len: int
+    num_q_heads: int
+    num_kv_heads: int
+    qk_nope_head_dim: int
+    kv_lora_rank: int
+    qk_rope_head_dim: int
+    kv_dtype: str
+    page_size: int
+
+    @property
+    def head_dim_qk(self) -> int:
+        return self.qk_nope_head_dim + self.qk_rope_head_dim
+
+    @property
+    def kv_bytes(self) -> int:
+        return self.batch_size * self.context_len * (self.kv_lora_rank + self.qk_rope_head_dim) * 2
+
+
+class B2DMlaKernel:
+    """Kernel(shape).run() adapter for absorbed MLA.  The shapes the library
+    builds: 128 query heads, one latent KV head of kv_lora_rank 512 + rope 64,
+    bf16, page size a multiple of 64.  softmax_scale = 1/sqrt(nope + rope), as
+    the reference passes as bmm1_scale (trtllm_mla_kernel.py:71)."""
+
+    def __init__(self, shape: MlaDecodeShape, seqlen_lo: Optional[int] = None,
+                 seqlen_hi: Optional[int] = None, page_perm: bool = False, seed: int = 0):
+        if not torch.cuda.is_available():
+            raise RuntimeError("CUDA is required")
+        if (shape.num_q_heads != 128 or shape.num_kv_heads != 1 or shape.kv_lora_rank != 512
+                or shape.qk_rope_head_dim != 64 or shape.kv_dtype != "bf16"
+                or shape.page_size % 64 != 0):
+            raise ValueError("b2d MLA decode is built for 128 heads, kv_lora_rank 512, rope 64, "
+                             "bf16, page size a multiple of 64")
+        self.shape = shape
+        lo = seqlen_lo if seqlen_lo is not None else shape.context_len
+        hi = seqlen_hi if seqlen_hi is not None else shape.context_len
+        self.workload = W.MlaWorkload("decodebench_mla", shape.batch_size, shape.num_q_heads,
+                                      shape.kv_lora_rank + shape.qk_rope_head_dim,
+                                      shape.kv_lora_rank, shape.page_size, lo, hi, seed=seed)
+        dev = torch.device("cuda")
+        self.x = W.make_mla_inputs(self.workload, dev, page_perm=page_perm)
+        self.scale = 1.0 / math.sqrt(shape.head_dim_qk)
+        self.out = torch.empty(shape.batch_size, shape.num_q_heads, shape.kv_lora_rank,
+                               dtype=torch.bfloat16, device=dev)
+        self.lse = torch.empty(shape.batch_size, shape.num_q_heads, dtype=torch.float32,
+                               device=dev)
+        self.workspace = api.DecodeWorkspace(dev)
+
+    def run(self):
+        x = self.x
+        return api.decode_mla(x["q"], x["kv_cache"], x["cache_seqlens"], x["block_table"],
+                              self.scale, head_dim_v=self.shape.kv_lora_rank, out=self.out,
+                              lse=self.lse, workspace=self.workspace)
+
+    @property
+    def algorithmic_bytes(self) -> int:
+        return W.mla_algorithmic_bytes(self.workload, self.x["cache_seqlens"].cpu())
+
+
 def cuda_time_ms(fn, repeat: int) -> list:
     """One CUDA-event pair per call, synchronised (flashinfer_benchmark.py:17-27)."""
     times = []
@@ -138,7 +210,84 @@ def parse_args(argv=None) -> argparse.Namespace:
     return ap.parse_args(argv)
 
 
+def parse_mla_args(argv=None) -> argparse.Namespace:
+    """Same flags and defaults as decodebench/trtllm_mla_benchmark.py:13-27."""
+    ap = argparse.ArgumentParser(description="Benchmark the b2d absorbed-MLA decode kernel.")
+    ap.add_argument("--batch-size", type=int, required=True)
+    ap.add_argument("--context-len", type=int, required=True)
+    ap.add_argument("--num-q-heads", type=int, required=True)
+    ap.add_argument("--num-kv-heads", type=int, default=1)
+    ap.add_argument("--qk-nope-head-dim", type=int, default=128)
+    ap.add_argument("--kv-lora-rank", type=int, default=512)
+    ap.add_argument("--qk-rope-head-dim", type=int, default=64)
+    ap.add_argument("--kv-dtype", required=True, choices=["bf16", "fp16"])
+    ap.add_argument("--page-size", type=int, default=64, choices=[64, 128])
+    ap.add_argument("--warmup-steps", type=int, default=10)
+    ap.add_argument("--repeat", type=int, default=50)
+    ap.add_argument("--output", type=Path, required=True)
+    ap.add_argument("--seqlen-lo", type=int, default=None)
+    ap.add_argument("--seqlen-hi", type=int, default=None)
+    ap.add_argument("--page-perm", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args(argv)
+
+
+def main_mla(argv=None) -> int:
+    args = parse_mla_args(argv)
+    shape = MlaDecodeShape(args.batch_size, args.context_len, args.num_q_heads,
+                           args.num_kv_heads, args.qk_nope_head_dim, args.kv_lora_rank,
+                           args.qk_rope_head_dim, args.kv_dtype, args.page_size)
+    kernel = B2DMlaKernel(shape, args.seqlen_lo, args.seqlen_hi, args.page_perm, args.seed)
+    for _ in range(args.warmup_steps):
+        kernel.run()
+    torch.cuda.synchronize()
+    times_ms = cuda_time_ms(kernel.run, args.repeat)
+    avg_ms = sum(times_ms) / len(times_ms)
+    p50_ms = percentile(times_ms, 50)
+    p95_ms = percentile(times_ms, 95)
+    alg = kernel.algorithmic_bytes
+    result = {
+        "run_id": os.environ.get("DECODEBENCH_RUN_ID"),
+        "timestamp": datetime.now(timezone.utc).isoformat(),
+        "gpu": torch.cuda.get_device_name(),
+        "backend": "b2d_mla_decode",
+        "kernel_path": "b2d mla_decode_kernel (sm_100a, tcgen05) via libb2d.so",
+        "layer": "kernel",
+        "workload_id": os.environ.get("DECODEBENCH_WORKLOAD_ID"),
+        "attention": "MLA",
+        "kv_dtype": shape.kv_dtype,
+        "page_size": shape.page_size,
+        "batch_size": shape.batch_size,
+        "context_len": shape.context_len,
+        "decode_steps": 1,
+        "kernel_latency_avg_us": avg_ms * 1000.0,
+        "kernel_latency_p50_us": p50_ms * 1000.0,
+        "kernel_latency_p95_us": p95_ms * 1000.0,
+        "approx_kv_bytes_read": shape.kv_bytes,
+        "approx_effective_kv_bandwidth_gb_s": shape.kv_bytes / (p50_ms * 1e6),
+        "peak_allocated_gb": torch.cuda.max_memory_allocated() / 1e9,
+        "selected_backend": "b2d_mla_decode",
+        "fallback": False,
+        "fallback_reason": None,
+        "notes": "Absorbed-MLA decode through b200decode.decode_mla (one C-ABI call per run).",
+        "roofline_bytes": alg,
+        "achieved_tb_s": alg / (p50_ms * 1e-3) / 1e12,
+        "seqlen_lo": kernel.workload.seqlen_lo,
+        "seqlen_hi": kernel.workload.seqlen_hi,
+        "seed": args.seed,
+        "page_perm": args.page_perm,
+    }
+    args.output.parent.mkdir(parents=True, exist_ok=True)
+    args.output.write_text(json.dumps(result, indent=2) + "\n", encoding="utf-8")
+    print(json.dumps(result))
+    return 0
+
+
 def main(argv=None) -> int:
+    import sys
+    argv = sys.argv[1:] if argv is None else list(argv)
+    if argv and argv[0] == "mla":
+        return main_mla(argv[1:])
     args = parse_args(argv)
     shape = DecodeShape(args.batch_size, args.context_len, args.num_q_heads, args.num_kv_heads,
                         args.head_dim, args.kv_dtype, args.page_size)

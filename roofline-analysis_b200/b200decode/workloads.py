@@ -153,13 +153,14 @@ def make_gqa_inputs(w: GqaWorkload, device="cpu", seqlens: Optional[torch.Tensor
                 k_scale=k_scale, v_scale=v_scale, softmax_scale=w.softmax_scale)
 
 
-def make_mla_inputs(w: MlaWorkload, device="cpu", seqlens: Optional[torch.Tensor] = None):
+def make_mla_inputs(w: MlaWorkload, device="cpu", seqlens: Optional[torch.Tensor] = None,
+                    page_perm: bool = True):
     """Inputs for decode_mla(): q [B, H, 576], kv_cache [pages, P, 576]."""
     device = torch.device(device)
     if seqlens is None:
         seqlens = draw_seqlens(w.batch, w.seqlen_lo, w.seqlen_hi, w.seed)
     w = w.scaled(batch=len(seqlens))
-    bt, npages = make_block_table(seqlens, w.page_size, True, w.seed)
+    bt, npages = make_block_table(seqlens, w.page_size, page_perm, w.seed)
     gen = torch.Generator(device=device).manual_seed(w.seed * 31 + 2)
     q = _randn((w.batch, w.num_heads, w.head_dim_qk), gen, device, w.value_std).to(torch.bfloat16)
     kv = torch.empty((npages, w.page_size, w.head_dim_qk), dtype=torch.bfloat16, device=device)

@@ -82,7 +82,11 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
   pl->group = group;
   const int es = kv_elem_bytes(a->kv_dtype);
   static const int use_mma = env_int("B2D_GQA_MMA", 1);
-  static const int hk_cap = env_int("B2D_GQA_HKMAX", 4);
+  // KV heads per tile: with 16-bit caches a whole token row of up to 8 heads
+  // (one contiguous 2 KB run per token at D = 128) streams best; fp8 tiles
+  // are half as wide and do better with more, smaller rows in flight.
+  static const int hk_cap_env = env_int("B2D_GQA_HKMAX", 0);
+  const int hk_cap = hk_cap_env > 0 ? hk_cap_env : (a->kv_dtype == B2D_FP8_E4M3 ? 4 : 8);
   // fp8 tiles use whole 128-byte lines per head row, so head_dim >= 128.
   pl->mma = use_mma && (a->page_size % 16 == 0) &&
             !(a->kv_dtype == B2D_FP8_E4M3 && a->head_dim < 128);
@@ -104,6 +108,17 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
     if (cap_hk < 1) cap_hk = 1;
     pl->hk = largest_divisor_leq(a->num_kv_heads, cap_hk);
     pl->T = 16;
+    // Small problems (few sequences, short caches): narrower tiles give more
+    // chunks, so every CTA still gets about two.  The chunk count is bounded
+    // by the block table's width; the lengths themselves live on the device.
+    if (hk_cap_env <= 0) {
+      int sms = 148;
+      device_sm_count(&sms);
+      const int64_t toks = (int64_t)a->max_pages_per_seq * a->page_size;
+      const int64_t per_head_row = (int64_t)a->batch * ((toks + 15) / 16);
+      while (pl->hk > 1 && per_head_row * (a->num_kv_heads / pl->hk) < 4LL * sms)
+        pl->hk = largest_divisor_leq(a->num_kv_heads, pl->hk / 2);
+    }
   } else {
     static const int hqw_cap = env_int("B2D_GQA_HQW", 2);
     pl->np = 0;

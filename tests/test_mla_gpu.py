@@ -95,3 +95,27 @@ def test_mla_rejects_unsupported_shapes(cuda):
     with pytest.raises(b200decode.B2DError):
         b200decode.decode_mla(x["q"][:, :64].contiguous(), x["kv_cache"], x["cache_seqlens"],
                               x["block_table"])
+
+
+def test_decodebench_mla_adapter(cuda, tmp_path):
+    """`python -m b200decode.decodebench mla ...` (trtllm_mla_benchmark.py's
+    flags and record); the adapter's run() output matches the oracle."""
+    import json
+    from b200decode import decodebench
+    shape = decodebench.MlaDecodeShape(2, 300, 128, 1, 128, 512, 64, "bf16", 64)
+    k = decodebench.B2DMlaKernel(shape, seed=1)
+    out, lse = k.run()
+    torch.cuda.synchronize()
+    x = dict(k.x, softmax_scale=k.scale)
+    assert_parity(out, lse, *_oracle(x))
+    with pytest.raises(ValueError):
+        decodebench.B2DMlaKernel(decodebench.MlaDecodeShape(2, 300, 64, 1, 128, 512, 64, "bf16", 64))
+    path = tmp_path / "m.json"
+    rc = decodebench.main(["mla", "--batch-size", "4", "--context-len", "1000", "--num-q-heads",
+                           "128", "--kv-dtype", "bf16", "--page-size", "64", "--warmup-steps", "2",
+                           "--repeat", "5", "--output", str(path)])
+    assert rc == 0
+    d = json.loads(path.read_text())
+    assert d["attention"] == "MLA" and d["approx_kv_bytes_read"] == 4 * 1000 * 576 * 2
+    for key in ("kernel_latency_p50_us", "approx_effective_kv_bandwidth_gb_s", "fallback"):
+        assert key in d
