@@ -66,6 +66,19 @@ enum b2d_flags {
   B2D_FLAG_COMBINE_ONLY = 2
 };
 
+/* Paged-cache layouts (b2d_gqa_args.kv_layout). */
+enum b2d_kv_layout {
+  /* [page, token, head, head_dim] in any order given by the strides: NHD
+   * [pages, P, Hkv, D], TRT-LLM HND [pages, 2, Hkv, P, D], ... */
+  B2D_KV_STRIDED = 0,
+  /* vLLM paged_attention: K [blocks, Hkv, D/8, P, 8] (8 elements = 16 bytes
+   * innermost), V [blocks, Hkv, D, P] (tokens innermost); each head's block
+   * contiguous, blocks of all heads contiguous (stride_page = Hkv *
+   * stride_head = Hkv * D * P elements).  16-bit caches, page_size % 16 == 0.
+   * The *_stride_tok fields are ignored. */
+  B2D_KV_VLLM = 1
+};
+
 /* Element types. */
 enum b2d_dtype {
   B2D_BF16 = 0,
@@ -117,7 +130,8 @@ typedef struct b2d_gqa_args {
   size_t workspace_bytes;
   int32_t num_ctas;        /* 0 = one resident wave on this device          */
   int32_t flags;           /* B2D_FLAG_* (0 = normal decode)                */
-  int32_t reserved[2];
+  int32_t kv_layout;       /* B2D_KV_* (0 = strided NHD/HND)                */
+  int32_t reserved;
 } b2d_gqa_args;
 
 /* Workspace bytes that b2d_decode_gqa needs for these arguments (pointers

@@ -10,6 +10,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_native" / "libb2d.so"
 
+B2D_KV_STRIDED, B2D_KV_VLLM = 0, 1
 B2D_BF16, B2D_FP16, B2D_FP8_E4M3, B2D_FP32 = 0, 1, 2, 3
 B2D_FLAG_SKIP_COMBINE, B2D_FLAG_COMBINE_ONLY = 1, 2
 
@@ -44,7 +45,8 @@ class GqaArgs(C.Structure):
         ("q_dtype", C.c_int32), ("kv_dtype", C.c_int32),
         ("softmax_scale", C.c_float),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
-        ("num_ctas", C.c_int32), ("flags", C.c_int32), ("reserved", C.c_int32 * 2),
+        ("num_ctas", C.c_int32), ("flags", C.c_int32), ("kv_layout", C.c_int32),
+        ("reserved", C.c_int32),
     ]
 
 

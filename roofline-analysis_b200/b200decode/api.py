@@ -96,7 +96,18 @@ def _gqa_args(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, k_
         raise ValueError(f"q must be [B, Hq, D] or [B, 1, Hq, D], got {tuple(q.shape)}")
     if q.dtype not in (torch.bfloat16, torch.float16):
         raise ValueError(f"q dtype must be bf16 or fp16, got {q.dtype}")
-    if k_cache.dim() != 4 or v_cache.dim() != 4 or k_cache.shape != v_cache.shape:
+    vllm = kv_layout == "vllm"
+    if vllm:
+        # vLLM paged_attention (decodebench/vllm_paged_kernel.py:102-123):
+        # K [blocks, Hkv, D/x, P, x] with x * elem = 16 bytes, V [blocks, Hkv, D, P]
+        if k_cache.dim() != 5 or v_cache.dim() != 4:
+            raise ValueError("kv_layout='vllm' takes K [blocks, Hkv, D/x, P, x] and V [blocks, Hkv, D, P]")
+        nb, hkv_, dx, page_, x = k_cache.shape
+        if x * k_cache.element_size() != 16 or tuple(v_cache.shape) != (nb, hkv_, dx * x, page_):
+            raise ValueError("vLLM cache shapes do not match (x must be 16 bytes of elements)")
+        if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+            raise ValueError("kv_layout='vllm' needs contiguous caches")
+    elif k_cache.dim() != 4 or v_cache.dim() != 4 or k_cache.shape != v_cache.shape:
         raise ValueError("k_cache and v_cache must be matching 4-D paged caches")
     if k_cache.dtype != v_cache.dtype or k_cache.dtype not in (q.dtype, torch.float8_e4m3fn):
         raise ValueError(f"cache dtype {k_cache.dtype} must equal q's {q.dtype} or be float8_e4m3fn")
@@ -108,10 +119,16 @@ def _gqa_args(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, k_
     if block_table.dim() != 2 or block_table.stride(1) != 1:
         raise ValueError("block_table must be [B, max_pages] with contiguous rows")
     bsz, hq, d = q.shape
-    ks_p, ks_t, ks_h, page, hkv = _layout_strides(k_cache, kv_layout)
-    vs_p, vs_t, vs_h, _, _ = _layout_strides(v_cache, kv_layout)
-    if k_cache.shape[-1] != d:
-        raise ValueError("head_dim mismatch between q and the caches")
+    if vllm:
+        ks_p, ks_t, ks_h, page, hkv = k_cache.stride(0), x, k_cache.stride(1), page_, hkv_
+        vs_p, vs_t, vs_h = v_cache.stride(0), 1, v_cache.stride(1)
+        if dx * x != d:
+            raise ValueError("head_dim mismatch between q and the caches")
+    else:
+        ks_p, ks_t, ks_h, page, hkv = _layout_strides(k_cache, kv_layout)
+        vs_p, vs_t, vs_h, _, _ = _layout_strides(v_cache, kv_layout)
+        if k_cache.shape[-1] != d:
+            raise ValueError("head_dim mismatch between q and the caches")
     if hq % hkv:
         raise ValueError(f"num_q_heads {hq} must be a multiple of num_kv_heads {hkv}")
     if cache_seqlens.shape != (bsz,) or block_table.shape[0] != bsz:
@@ -138,6 +155,7 @@ def _gqa_args(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, k_
     a.q_dtype, a.kv_dtype = _DT[q.dtype], _DT[k_cache.dtype]
     a.softmax_scale = float(softmax_scale)
     a.num_ctas = int(num_ctas or 0)
+    a.kv_layout = _lib.B2D_KV_VLLM if vllm else _lib.B2D_KV_STRIDED
     return a
 
 
@@ -152,7 +170,9 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
 
     q: [B, Hq, D] or [B, 1, Hq, D] (bf16/fp16).  k_cache, v_cache:
     [num_pages, P, Hkv, D] ("NHD") or [num_pages, Hkv, P, D] ("HND"), in q's
-    dtype or float8_e4m3fn with fp32 per-KV-head k_scale/v_scale.
+    dtype or float8_e4m3fn with fp32 per-KV-head k_scale/v_scale; or vLLM's
+    own layout ("vllm", 16-bit caches, P % 16 == 0): k_cache [blocks, Hkv,
+    D/8, P, 8], v_cache [blocks, Hkv, D, P].
     cache_seqlens: int32 [B]; block_table: int32 [B, max_pages].
     softmax_scale defaults to 1/sqrt(D).  Returns out (shape of q, q's dtype)
     and lse [B, Hq] fp32 (natural log).  `flags` (B2D_FLAG_*) exists for

@@ -71,7 +71,7 @@ class B2DDecodeKernel:
 
     def __init__(self, shape: DecodeShape, seqlen_lo: Optional[int] = None,
                  seqlen_hi: Optional[int] = None, page_perm: bool = False, seed: int = 0,
-                 kv_scale_range=None, use_graph: bool = False):
+                 kv_scale_range=None, use_graph: bool = False, kv_layout: str = "NHD"):
         if not torch.cuda.is_available():
             raise RuntimeError("CUDA is required")
         self.shape = shape
@@ -85,9 +85,17 @@ class B2DDecodeKernel:
             page_perm=page_perm, kv_scale_range=(kv_scale_range or ((1.0, 1.0) if fp8 else None)))
         self.x = W.make_gqa_inputs(self.workload, torch.device("cuda"))
         x = self.x
-        self.decoder = api.GqaDecoder(x["q"], x["k_cache"], x["v_cache"], x["cache_seqlens"],
-                                      x["block_table"], x["softmax_scale"], k_scale=x["k_scale"],
-                                      v_scale=x["v_scale"])
+        kc, vc = x["k_cache"], x["v_cache"]
+        if kv_layout == "HND":
+            kc, vc = kc.transpose(1, 2).contiguous(), vc.transpose(1, 2).contiguous()
+        elif kv_layout == "vllm":
+            kc, vc = W.to_vllm_layout(kc, vc)
+        elif kv_layout != "NHD":
+            raise ValueError(f"unknown kv_layout {kv_layout!r}")
+        self.kv_layout = kv_layout
+        self.decoder = api.GqaDecoder(x["q"], kc, vc, x["cache_seqlens"], x["block_table"],
+                                      x["softmax_scale"], k_scale=x["k_scale"],
+                                      v_scale=x["v_scale"], kv_layout=kv_layout)
         self.use_graph = use_graph
         if use_graph:
             self.decoder.capture()
@@ -207,6 +215,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--page-perm", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cuda-graph", action="store_true")
+    ap.add_argument("--kv-layout", default="NHD", choices=["NHD", "HND", "vllm"],
+                    help="cache layout handed to the kernel (vllm = paged_attention's "
+                         "K [blocks, Hkv, D/8, P, 8], V [blocks, Hkv, D, P])")
     return ap.parse_args(argv)
 
 
@@ -292,7 +303,7 @@ def main(argv=None) -> int:
     shape = DecodeShape(args.batch_size, args.context_len, args.num_q_heads, args.num_kv_heads,
                         args.head_dim, args.kv_dtype, args.page_size)
     kernel = B2DDecodeKernel(shape, args.seqlen_lo, args.seqlen_hi, args.page_perm, args.seed,
-                             use_graph=args.cuda_graph)
+                             use_graph=args.cuda_graph, kv_layout=args.kv_layout)
     for _ in range(args.warmup_steps):
         kernel.run()
     torch.cuda.synchronize()
@@ -334,6 +345,7 @@ def main(argv=None) -> int:
         "seed": args.seed,
         "page_perm": args.page_perm,
         "cuda_graph": args.cuda_graph,
+        "kv_layout": args.kv_layout,
     }
     args.output.parent.mkdir(parents=True, exist_ok=True)
     args.output.write_text(json.dumps(result, indent=2) + "\n", encoding="utf-8")

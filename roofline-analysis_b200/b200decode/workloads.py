@@ -153,6 +153,17 @@ def make_gqa_inputs(w: GqaWorkload, device="cpu", seqlens: Optional[torch.Tensor
                 k_scale=k_scale, v_scale=v_scale, softmax_scale=w.softmax_scale)
 
 
+def to_vllm_layout(k_cache: torch.Tensor, v_cache: torch.Tensor):
+    """NHD caches [pages, P, Hkv, D] -> vLLM paged_attention's layout
+    (decodebench/vllm_paged_kernel.py:102-123): K [pages, Hkv, D/x, P, x]
+    with x = 16 bytes of elements, V [pages, Hkv, D, P]."""
+    pages, P, hkv, d = k_cache.shape
+    x = 16 // k_cache.element_size()
+    k = k_cache.reshape(pages, P, hkv, d // x, x).permute(0, 2, 3, 1, 4).contiguous()
+    v = v_cache.permute(0, 2, 3, 1).contiguous()
+    return k, v
+
+
 def make_mla_inputs(w: MlaWorkload, device="cpu", seqlens: Optional[torch.Tensor] = None,
                     page_perm: bool = True):
     """Inputs for decode_mla(): q [B, H, 576], kv_cache [pages, P, 576]."""

@@ -57,6 +57,19 @@ static int validate(const b2d_gqa_args* a, bool need_pointers) {
   const int group = a->num_q_heads / a->num_kv_heads;
   if (group > 32) return B2D_ERR_UNSUPPORTED;
   if (a->page_size > (1 << 24)) return B2D_ERR_TOO_LARGE;
+  if (a->kv_layout != B2D_KV_STRIDED && a->kv_layout != B2D_KV_VLLM) return B2D_ERR_INVALID_ARG;
+  if (a->kv_layout == B2D_KV_VLLM) {
+    // K [blocks, Hkv, D/8, P, 8] and V [blocks, Hkv, D, P]: the kernel reads
+    // (block, head) as one flattened index, so blocks must be dense.
+    if (a->kv_dtype == B2D_FP8_E4M3 || a->page_size % 16 != 0) return B2D_ERR_UNSUPPORTED;
+    if (need_pointers) {
+      const int64_t blk = (int64_t)a->head_dim * a->page_size;
+      if (a->k_stride_head != blk || a->v_stride_head != blk ||
+          a->k_stride_page != blk * a->num_kv_heads || a->v_stride_page != blk * a->num_kv_heads)
+        return B2D_ERR_INVALID_ARG;
+      if (a->num_pages * a->num_kv_heads > (int64_t)INT32_MAX) return B2D_ERR_TOO_LARGE;
+    }
+  }
   if (!need_pointers) return B2D_OK;
   if (a->batch == 0) return B2D_OK;
   if (!a->q || !a->k_cache || !a->v_cache || !a->cache_seqlens || !a->block_table || !a->out)
@@ -69,8 +82,10 @@ static int validate(const b2d_gqa_args* a, bool need_pointers) {
     return B2D_ERR_ALIGNMENT;
   const int64_t strides[6] = {a->k_stride_page, a->k_stride_tok, a->k_stride_head,
                               a->v_stride_page, a->v_stride_tok, a->v_stride_head};
-  for (int64_t s : strides)
-    if (s <= 0 || (s * es) % 16 != 0) return B2D_ERR_ALIGNMENT;
+  for (int i = 0; i < 6; ++i) {
+    if (a->kv_layout == B2D_KV_VLLM && (i == 1 || i == 4)) continue;  // token strides implied
+    if (strides[i] <= 0 || (strides[i] * es) % 16 != 0) return B2D_ERR_ALIGNMENT;
+  }
   if ((a->q_stride_b * 2) % 16 || (a->q_stride_h * 2) % 16 || (a->out_stride_b * 2) % 16 ||
       (a->out_stride_h * 2) % 16)
     return B2D_ERR_ALIGNMENT;
@@ -93,6 +108,7 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
   // head_dim 192 is built for the tensor-core path with 16-bit caches only
   // (fp8 tiles need whole 128-byte lines per head row: head_dim % 128 == 0).
   if (a->head_dim == 192 && (!pl->mma || a->kv_dtype == B2D_FP8_E4M3)) return B2D_ERR_UNSUPPORTED;
+  if (a->kv_layout == B2D_KV_VLLM && !pl->mma) return B2D_ERR_UNSUPPORTED;
   if (pl->mma) {
     // Tensor-core consumer: a warp takes GW <= 16 query heads (<= 8 at
     // head_dim 192 and 256, to bound the accumulator registers) of one KV head; a
@@ -208,17 +224,17 @@ static int launch_t(const GqaPlan& pl, const CUtensorMap& tk, const CUtensorMap&
                   st, flags);
 }
 
-template <int D, int KIND, typename QT>
+template <int D, int KIND, typename QT, bool VL = false>
 static int launch_mma(const GqaPlan& pl, const CUtensorMap& tk, const CUtensorMap& tv,
                       const GqaParams& p, cudaStream_t st, int flags) {
   if (pl.np == 2) {
     if constexpr (D >= 192) return B2D_ERR_UNSUPPORTED;
     else
-      return launch_k(gqa_mma_kernel<D, KIND, QT, 2>, gqa_combine_kernel<D, QT>, pl, tk, tv, p,
-                      st, flags);
+      return launch_k(gqa_mma_kernel<D, KIND, QT, 2, VL>, gqa_combine_kernel<D, QT>, pl, tk, tv,
+                      p, st, flags);
   }
-  return launch_k(gqa_mma_kernel<D, KIND, QT, 1>, gqa_combine_kernel<D, QT>, pl, tk, tv, p, st,
-                  flags);
+  return launch_k(gqa_mma_kernel<D, KIND, QT, 1, VL>, gqa_combine_kernel<D, QT>, pl, tk, tv, p,
+                  st, flags);
 }
 
 template <int D, int KIND, typename QT>
@@ -236,6 +252,9 @@ static int launch_d(const b2d_gqa_args* a, const GqaPlan& pl, const CUtensorMap&
                     const CUtensorMap& tv, const GqaParams& p, cudaStream_t st) {
   const int flags = a->flags;
   const bool qbf = a->q_dtype == B2D_BF16;
+  if (a->kv_layout == B2D_KV_VLLM)  // the plan admits only 16-bit caches here
+    return qbf ? launch_mma<D, kKvBf16, __nv_bfloat16, true>(pl, tk, tv, p, st, flags)
+               : launch_mma<D, kKvFp16, __half, true>(pl, tk, tv, p, st, flags);
   if constexpr (D == 192) {
     // the plan admits only the tensor-core path with 16-bit caches here
     return qbf ? launch_mma<D, kKvBf16, __nv_bfloat16>(pl, tk, tv, p, st, flags)
@@ -258,9 +277,39 @@ static int launch_d(const b2d_gqa_args* a, const GqaPlan& pl, const CUtensorMap&
 }
 
 static int encode_kv_map(CUtensorMap* map, const void* base, const b2d_gqa_args* a,
-                         int64_t s_page, int64_t s_tok, int64_t s_head, const GqaPlan& pl) {
+                         int64_t s_page, int64_t s_tok, int64_t s_head, const GqaPlan& pl,
+                         bool is_v) {
   const int es = kv_elem_bytes(a->kv_dtype);
   const CUtensorMapDataType dt = es == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  const uint64_t page_heads = (uint64_t)a->num_pages * (uint64_t)a->num_kv_heads;
+  if (a->kv_layout == B2D_KV_VLLM && !is_v) {
+    // K [blocks, Hkv, D/8, P, 8]: 16 tokens x 8 elements are one contiguous
+    // 256-byte run, so the map is {P * 8 elements, 8-dim group, block * Hkv +
+    // head} with a 128-element inner box; shared layout [HK][D / 8][16
+    // tokens][8], no swizzle (an ldmatrix's 8 token rows are 16 bytes apart).
+    const uint64_t P = (uint64_t)a->page_size;
+    const uint64_t dims[3] = {P * 8, (uint64_t)a->head_dim / 8, page_heads};
+    const uint64_t strides[2] = {P * 16, (uint64_t)(s_head * es)};
+    const uint32_t box[3] = {128u, (uint32_t)(a->head_dim / 8), (uint32_t)pl.hk};
+    return encode_tiled_map(map, dt, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (a->kv_layout == B2D_KV_VLLM) {
+    // V [blocks, Hkv, D, P]: shared layout [HK][D][16 tokens] (32-byte rows =
+    // V^T), no swizzle.  With 16-token pages a head's block is one
+    // contiguous run: {8 dims x 16 tokens, 8-dim group, block * Hkv + head};
+    // otherwise {token, dim, block * Hkv + head} with 32-byte rows.
+    const uint64_t P = (uint64_t)a->page_size;
+    if (P == 16) {
+      const uint64_t dims[3] = {128, (uint64_t)a->head_dim / 8, page_heads};
+      const uint64_t strides[2] = {256, (uint64_t)(s_head * es)};
+      const uint32_t box[3] = {128u, (uint32_t)(a->head_dim / 8), (uint32_t)pl.hk};
+      return encode_tiled_map(map, dt, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    const uint64_t dims[3] = {P, (uint64_t)a->head_dim, page_heads};
+    const uint64_t strides[2] = {P * 2, (uint64_t)(s_head * es)};
+    const uint32_t box[3] = {16u, (uint32_t)a->head_dim, (uint32_t)pl.hk};
+    return encode_tiled_map(map, dt, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
   if (pl.mma) {
     // {128-byte line, token, line of the head row, head, page}; 128-byte
     // swizzle.  Shared layout: [HK][D / line][16 tokens][line].
@@ -319,8 +368,10 @@ extern "C" int b2d_decode_gqa(const b2d_gqa_args* a, void* stream) {
   if (!a->workspace || a->workspace_bytes < pl.ws_bytes) return B2D_ERR_WORKSPACE;
   if ((uintptr_t)a->workspace & 255) return B2D_ERR_ALIGNMENT;
   CUtensorMap tk, tv;
-  if (encode_kv_map(&tk, a->k_cache, a, a->k_stride_page, a->k_stride_tok, a->k_stride_head, pl) ||
-      encode_kv_map(&tv, a->v_cache, a, a->v_stride_page, a->v_stride_tok, a->v_stride_head, pl))
+  if (encode_kv_map(&tk, a->k_cache, a, a->k_stride_page, a->k_stride_tok, a->k_stride_head, pl,
+                    false) ||
+      encode_kv_map(&tv, a->v_cache, a, a->v_stride_page, a->v_stride_tok, a->v_stride_head, pl,
+                    true))
     return B2D_ERR_CUDA;
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -107,6 +107,17 @@ __device__ __forceinline__ void tma_load_5d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 3-D tiled TMA load (no multicast).
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)),
+      "l"(policy)
+      : "memory");
+}
+
 // Byte address of (line, 16-byte chunk) under the 128-byte TMA swizzle.
 __device__ __forceinline__ uint32_t swz(uint32_t base, int line, int chunk) {
   return base + (uint32_t)(line * 128) + (uint32_t)(((chunk ^ (line & 7)) & 7) << 4);
@@ -118,7 +129,12 @@ __device__ __forceinline__ float q_at(const QT* qrow, bool valid, int dim) {
   return valid ? static_cast<float>(qrow[dim]) : 0.f;
 }
 
-template <int D, int KIND, typename QT, int NP>
+// VL: vLLM cache layout (K [blocks, Hkv, D/8, P, 8], V [blocks, Hkv, D, P]).
+// K tiles arrive as [head][D/8][16 tokens][8 elements] (no swizzle: an
+// ldmatrix's 8 token rows are 16 bytes apart); V tiles arrive transposed
+// ([head][D][16 tokens], 32-byte rows, no swizzle) and feed the P.V product
+// through plain (non-transposing) ldmatrix.
+template <int D, int KIND, typename QT, int NP, bool VL = false>
 __global__ void __launch_bounds__(32 * 9, 1)
     gqa_mma_kernel(const __grid_constant__ CUtensorMap tmap_k,
                    const __grid_constant__ CUtensorMap tmap_v, const GqaParams p) {
@@ -201,8 +217,15 @@ __global__ void __launch_bounds__(32 * 9, 1)
           } else {
             uint8_t* kdst = tiles + (size_t)s * 2 * p.stage_bytes;
             mbar_arrive_expect_tx(full + s, 2u * p.stage_bytes);
-            tma_load_5d(kdst, &tmap_k, full + s, off, 0, h0, page, policy);
-            tma_load_5d(kdst + p.stage_bytes, &tmap_v, full + s, off, 0, h0, page, policy);
+            if constexpr (VL) {
+              const int ph_idx = page * p.Hkv + h0;   // flattened (block, head)
+              tma_load_3d(kdst, &tmap_k, full + s, off * 8, 0, ph_idx, policy);
+              tma_load_3d(kdst + p.stage_bytes, &tmap_v, full + s, p.P == 16 ? 0 : off, 0, ph_idx,
+                          policy);
+            } else {
+              tma_load_5d(kdst, &tmap_k, full + s, off, 0, h0, page, policy);
+              tma_load_5d(kdst + p.stage_bytes, &tmap_v, full + s, off, 0, h0, page, policy);
+            }
           }
         }
         if (++s == p.stages) {
@@ -341,7 +364,16 @@ __global__ void __launch_bounds__(32 * 9, 1)
     const uint32_t kb = tiles_u32 + (uint32_t)s * 2u * p.stage_bytes;
     const uint32_t vb = kb + p.stage_bytes;
 
-    if (nvalid < T) {
+    if (VL && nvalid < T) {
+      // Same for the transposed V tile: elements (dim, token >= nvalid).
+      const uint32_t vbh = vb + (uint32_t)(hk * D * 32);
+      for (int idx = lane; idx < D * (T - nvalid); idx += 32) {
+        const int dim = idx / (T - nvalid), tk = nvalid + idx % (T - nvalid);
+        const uint32_t a = vbh + (uint32_t)(dim * 32 + tk * 2);
+        asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"((unsigned short)0) : "memory");
+      }
+      __syncwarp();
+    } else if (nvalid < T) {
       // Token slots past the sequence end (same page) may hold anything, even
       // NaN: zero those V lines of this head so P = 0 multiplies zeros.
       for (int idx = lane; idx < DC * (T - nvalid) * 8; idx += 32) {
@@ -366,9 +398,13 @@ __global__ void __launch_bounds__(32 * 9, 1)
         for (int j = 0; j < 2; ++j) {
           const int mtx = lane >> 3, rr = lane & 7;
           const int dim = 32 * kk + 8 * mtx;
-          const int line = line0 + (dim / LINE) * T + 8 * j + rr;
           uint32_t bfr[4];
-          ldsm_x4(swz(kb, line, (dim % LINE) / 8), bfr);
+          if constexpr (VL) {
+            ldsm_x4(kb + (uint32_t)(hk * D * 32 + ((dim / 8) * 16 + 8 * j + rr) * 16), bfr);
+          } else {
+            const int line = line0 + (dim / LINE) * T + 8 * j + rr;
+            ldsm_x4(swz(kb, line, (dim % LINE) / 8), bfr);
+          }
           uint32_t a0[4], a1[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -455,7 +491,20 @@ __global__ void __launch_bounds__(32 * 9, 1)
     }
 
     // ---- O^T += V^T . P ----
-    if constexpr (!FP8) {
+    if constexpr (VL) {
+      // V^T rows are dims: matrices (dims 0-7 | 8-15) x (tokens 0-7 | 8-15)
+      // give the A fragment directly.
+      const uint32_t vbh = vb + (uint32_t)(hk * D * 32);
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        const int mtx = lane >> 3, rr = lane & 7;
+        const int dim = 16 * i + 8 * (mtx & 1) + rr;
+        uint32_t afr[4];
+        ldsm_x4(vbh + (uint32_t)(dim * 32 + (mtx >> 1) * 16), afr);
+#pragma unroll
+        for (int n = 0; n < NP; ++n) mma16816<MMA_BF16>(acc[n][i], afr, pb[n][0], pb[n][1]);
+      }
+    } else if constexpr (!FP8) {
 #pragma unroll
       for (int i = 0; i < MT; ++i) {
         const int mtx = lane >> 3, rr = lane & 7;

@@ -74,6 +74,9 @@ def test_workspace_query_and_plan_on_host():
     (dict(head_dim=96), -2),                 # unsupported head_dim
     (dict(head_dim=192, kv_dtype=_lib.B2D_FP8_E4M3), -2),  # fp8 needs head_dim % 128 == 0
     (dict(head_dim=192, page_size=8), -2),   # 192 only on the tensor-core path (page % 16)
+    (dict(kv_layout=_lib.B2D_KV_VLLM, kv_dtype=_lib.B2D_FP8_E4M3), -2),  # vLLM layout: 16-bit
+    (dict(kv_layout=_lib.B2D_KV_VLLM, page_size=8), -2),                # ... and page % 16
+    (dict(kv_layout=7), -1),                 # unknown layout
     (dict(num_q_heads=30), -1),              # not a multiple of num_kv_heads
     (dict(q_dtype=_lib.B2D_FP8_E4M3), -2),   # q must be 16-bit
     (dict(kv_dtype=_lib.B2D_FP16), -2),      # cache must match q or be fp8

@@ -121,6 +121,44 @@ def test_hnd_layout_and_strided_views(cuda):
     assert_parity(out, lse, *oracle_gqa(x))
 
 
+@pytest.mark.parametrize("dt", ["bf16", "fp16"])
+@pytest.mark.parametrize("d,hq,hkv,page", [(128, 32, 8, 16), (128, 8, 2, 64), (64, 16, 4, 32),
+                                           (256, 8, 1, 16), (192, 8, 2, 16), (128, 32, 32, 16)])
+def test_vllm_cache_layout(cuda, dt, d, hq, hkv, page):
+    """vLLM paged_attention's own cache layout (K [blocks, Hkv, D/x, P, x],
+    V [blocks, Hkv, D, P]; decodebench/vllm_paged_kernel.py:102-123) gives
+    the same decode as the NHD copy of the same cache."""
+    w = SMALL.scaled(head_dim=d, kv_dtype=dt, q_dtype=dt, num_q_heads=hq, num_kv_heads=hkv,
+                     page_size=page)
+    x = _inputs(cuda, w, lens=[1, page - 1, 3 * page + 5, 300, 0])
+    kv, vv = W.to_vllm_layout(x["k_cache"], x["v_cache"])
+    out, lse = b200decode.decode(x["q"], kv, vv, x["cache_seqlens"], x["block_table"],
+                                 x["softmax_scale"], kv_layout="vllm")
+    torch.cuda.synchronize()
+    b200decode.check_device_status()
+    assert_parity(out, lse, *oracle_gqa(x))
+
+
+def test_vllm_cache_layout_decoder_and_refusals(cuda):
+    x = _inputs(cuda, SMALL.scaled(num_q_heads=16, num_kv_heads=4))
+    kv, vv = W.to_vllm_layout(x["k_cache"], x["v_cache"])
+    dec = b200decode.GqaDecoder(x["q"], kv, vv, x["cache_seqlens"], x["block_table"],
+                                x["softmax_scale"], kv_layout="vllm")
+    dec.capture()
+    out, lse = dec.replay()
+    torch.cuda.synchronize()
+    assert_parity(out, lse, *oracle_gqa(x))
+    # page size 8 is not a multiple of 16: refused, not computed wrongly
+    x8 = _inputs(cuda, SMALL.scaled(page_size=8))
+    k8, v8 = W.to_vllm_layout(x8["k_cache"], x8["v_cache"])
+    with pytest.raises(b200decode.B2DError, match="(?i)unsupported"):
+        b200decode.decode(x8["q"], k8, v8, x8["cache_seqlens"], x8["block_table"],
+                          kv_layout="vllm")
+    with pytest.raises(ValueError):
+        b200decode.decode(x["q"], kv[:, :, :, :, :4], vv, x["cache_seqlens"], x["block_table"],
+                          kv_layout="vllm")
+
+
 def test_q_with_token_axis_and_preallocated_outputs(cuda):
     x = _inputs(cuda, SMALL)
     q4 = x["q"][:, None]
