@@ -221,7 +221,9 @@ typedef struct b2d_append_args {
   int* bad_slots;
   int32_t num_tokens, num_kv_heads, head_dim, page_size;
   int32_t src_dtype, cache_dtype;
-  int32_t reserved[2];
+  int32_t kv_layout;       /* B2D_KV_* ; for B2D_KV_VLLM only the page and
+                              head strides are read (16-bit caches)         */
+  int32_t reserved;
 } b2d_append_args;
 
 int b2d_append_kv(const b2d_append_args* args, void* stream);

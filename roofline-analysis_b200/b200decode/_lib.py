@@ -78,7 +78,7 @@ class AppendArgs(C.Structure):
         ("k_scale", C.c_void_p), ("v_scale", C.c_void_p), ("bad_slots", C.c_void_p),
         ("num_tokens", C.c_int32), ("num_kv_heads", C.c_int32), ("head_dim", C.c_int32),
         ("page_size", C.c_int32), ("src_dtype", C.c_int32), ("cache_dtype", C.c_int32),
-        ("reserved", C.c_int32 * 2),
+        ("kv_layout", C.c_int32), ("reserved", C.c_int32),
     ]
 
 

@@ -336,7 +336,9 @@ def append_kv(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_c
     key, value: [T, Hkv, D] bf16/fp16; slot_mapping: int64 [T] with slot =
     page * P + offset (negative = skip).  Caches in the source dtype, or
     float8_e4m3fn: stored value = e4m3(x / scale[head]) (round-to-nearest-even,
-    saturated).  bad_slots: optional int32 [1] counter of out-of-range slots."""
+    saturated).  kv_layout "NHD", "HND" or "vllm" (paged_attention's K
+    [blocks, Hkv, D/8, P, 8] and V [blocks, Hkv, D, P], 16-bit caches).
+    bad_slots: optional int32 [1] counter of out-of-range slots."""
     if not key.is_cuda:
         raise RuntimeError("append_kv needs CUDA tensors (there is no CPU path)")
     lib = _lib.load()
@@ -350,10 +352,21 @@ def append_kv(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_c
         raise ValueError("slot_mapping must be int64 [T]")
     if k_cache.dtype != v_cache.dtype or k_cache.dtype not in (key.dtype, torch.float8_e4m3fn):
         raise ValueError("caches must be in the source dtype or float8_e4m3fn")
-    ks_p, ks_t, ks_h, page, hkv = _layout_strides(k_cache, kv_layout)
-    vs_p, vs_t, vs_h, _, _ = _layout_strides(v_cache, kv_layout)
-    if hkv != key.shape[1] or k_cache.shape[-1] != key.shape[2]:
-        raise ValueError("cache heads / head_dim do not match key")
+    vllm = kv_layout == "vllm"
+    if vllm:   # K [blocks, Hkv, D/8, P, 8], V [blocks, Hkv, D, P] (16-bit caches)
+        if (k_cache.dim() != 5 or v_cache.dim() != 4 or k_cache.shape[-1] * k_cache.element_size() != 16
+                or not (k_cache.is_contiguous() and v_cache.is_contiguous())):
+            raise ValueError("kv_layout='vllm' takes contiguous K [blocks, Hkv, D/x, P, x] and V [blocks, Hkv, D, P]")
+        nb, hkv, dx, page, x = k_cache.shape
+        if tuple(v_cache.shape) != (nb, hkv, dx * x, page) or dx * x != key.shape[2] or hkv != key.shape[1]:
+            raise ValueError("vLLM cache shapes do not match key")
+        ks_p, ks_t, ks_h = k_cache.stride(0), x, k_cache.stride(1)
+        vs_p, vs_t, vs_h = v_cache.stride(0), 1, v_cache.stride(1)
+    else:
+        ks_p, ks_t, ks_h, page, hkv = _layout_strides(k_cache, kv_layout)
+        vs_p, vs_t, vs_h, _, _ = _layout_strides(v_cache, kv_layout)
+        if hkv != key.shape[1] or k_cache.shape[-1] != key.shape[2]:
+            raise ValueError("cache heads / head_dim do not match key")
     a = _lib.AppendArgs()
     a.key, a.value = key.data_ptr(), value.data_ptr()
     a.src_stride_t, a.src_stride_h = key.stride(0), key.stride(1)
@@ -368,6 +381,7 @@ def append_kv(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_c
     a.bad_slots = _ptr(bad_slots)
     a.num_tokens, a.num_kv_heads, a.head_dim, a.page_size = key.shape[0], hkv, key.shape[2], page
     a.src_dtype, a.cache_dtype = _DT[key.dtype], _DT[k_cache.dtype]
+    a.kv_layout = _lib.B2D_KV_VLLM if vllm else _lib.B2D_KV_STRIDED
     stream = torch.cuda.current_stream(key.device).cuda_stream
     _check(lib.b2d_append_kv(C.byref(a), C.c_void_p(stream)), "b2d_append_kv")
 

@@ -17,6 +17,8 @@ struct AppendParams {
   void* kc;
   void* vc;
   int64_t k_sp, k_st, k_sh, v_sp, v_st, v_sh;
+  int64_t k_sg;   // elements between consecutive 8-element groups of a K row (8, or P * 8 for vLLM)
+  int64_t v_sd;   // elements between consecutive dims of a V row (1, or P for vLLM)
   const int64_t* slots;
   const float* k_scale;
   const float* v_scale;
@@ -52,11 +54,19 @@ __global__ void __launch_bounds__(256) append_kv_kernel(const AppendParams p) {
   const int64_t src = (int64_t)t * p.src_st + (int64_t)h * p.src_sh + c * 8;
   const uint4 kw = *reinterpret_cast<const uint4*>(static_cast<const ST*>(p.key) + src);
   const uint4 vw = *reinterpret_cast<const uint4*>(static_cast<const ST*>(p.value) + src);
-  const int64_t kd = page * p.k_sp + off * p.k_st + (int64_t)h * p.k_sh + c * 8;
-  const int64_t vd = page * p.v_sp + off * p.v_st + (int64_t)h * p.v_sh + c * 8;
+  const int64_t kd = page * p.k_sp + off * p.k_st + (int64_t)h * p.k_sh + c * p.k_sg;
+  const int64_t vd = page * p.v_sp + off * p.v_st + (int64_t)h * p.v_sh + c * 8 * p.v_sd;
   if constexpr (!FP8) {
     *reinterpret_cast<uint4*>(static_cast<ST*>(p.kc) + kd) = kw;
-    *reinterpret_cast<uint4*>(static_cast<ST*>(p.vc) + vd) = vw;
+    if (p.v_sd == 1) {
+      *reinterpret_cast<uint4*>(static_cast<ST*>(p.vc) + vd) = vw;
+    } else {
+      // vLLM's V is [blocks, Hkv, D, P]: the 8 dims of this row are P apart.
+      const uint16_t* e = reinterpret_cast<const uint16_t*>(&vw);
+      uint16_t* dst = reinterpret_cast<uint16_t*>(static_cast<ST*>(p.vc) + vd);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dst[i * p.v_sd] = e[i];
+    }
   } else {
     const float ks = 1.f / (p.k_scale ? __ldg(p.k_scale + h) : 1.f);
     const float vs = 1.f / (p.v_scale ? __ldg(p.v_scale + h) : 1.f);
@@ -98,14 +108,19 @@ extern "C" int b2d_append_kv(const b2d_append_args* a, void* stream) {
   if (a->num_tokens == 0) return B2D_OK;
   if (!a->key || !a->value || !a->k_cache || !a->v_cache || !a->slot_mapping || a->num_pages <= 0)
     return B2D_ERR_INVALID_ARG;
+  if (a->kv_layout != B2D_KV_STRIDED && a->kv_layout != B2D_KV_VLLM) return B2D_ERR_INVALID_ARG;
+  const bool vllm = a->kv_layout == B2D_KV_VLLM;
+  if (vllm && a->cache_dtype == B2D_FP8_E4M3) return B2D_ERR_UNSUPPORTED;
   const int es = a->cache_dtype == B2D_FP8_E4M3 ? 1 : 2;
   if (((uintptr_t)a->key & 15) || ((uintptr_t)a->value & 15) || ((uintptr_t)a->k_cache & 15) ||
       ((uintptr_t)a->v_cache & 15))
     return B2D_ERR_ALIGNMENT;
   const int64_t cs[6] = {a->k_stride_page, a->k_stride_tok, a->k_stride_head,
                          a->v_stride_page, a->v_stride_tok, a->v_stride_head};
-  for (int64_t s : cs)
-    if (s <= 0 || (s * es) % 8 != 0) return B2D_ERR_ALIGNMENT;
+  for (int i = 0; i < 6; ++i) {
+    if (vllm && (i == 1 || i == 4)) continue;  // token strides implied by the layout
+    if (cs[i] <= 0 || (cs[i] * es) % 8 != 0) return B2D_ERR_ALIGNMENT;
+  }
   if ((a->src_stride_t * 2) % 16 || (a->src_stride_h * 2) % 16) return B2D_ERR_ALIGNMENT;
   AppendParams p{};
   p.key = a->key;
@@ -120,6 +135,14 @@ extern "C" int b2d_append_kv(const b2d_append_args* a, void* stream) {
   p.v_sp = a->v_stride_page;
   p.v_st = a->v_stride_tok;
   p.v_sh = a->v_stride_head;
+  p.k_sg = 8;
+  p.v_sd = 1;
+  if (vllm) {  // K [blocks, Hkv, D/8, P, 8], V [blocks, Hkv, D, P]
+    p.k_st = 8;
+    p.k_sg = (int64_t)a->page_size * 8;
+    p.v_st = 1;
+    p.v_sd = a->page_size;
+  }
   p.slots = a->slot_mapping;
   p.k_scale = a->k_scale;
   p.v_scale = a->v_scale;

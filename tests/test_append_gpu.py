@@ -75,3 +75,41 @@ def test_append_then_decode_round_trip(cuda):
                                          v_scale=x["v_scale"])
     torch.cuda.synchronize()
     assert (out.float() - ref_out.float()).abs().max().item() < 2e-2
+
+
+def test_append_vllm_layout_bit_exact_and_round_trip(cuda):
+    """reshape_and_cache into vLLM paged_attention's own layout (K [blocks,
+    Hkv, D/8, P, 8], V [blocks, Hkv, D, P]) writes the same values as the NHD
+    oracle, and decoding those caches with kv_layout="vllm" matches."""
+    g = torch.Generator(device=cuda).manual_seed(2)
+    T, H, D, P, pages = 45, 2, 128, 16, 6
+    key = torch.randn(T, H, D, generator=g, device=cuda).to(torch.bfloat16)
+    val = torch.randn(T, H, D, generator=g, device=cuda).to(torch.bfloat16)
+    kc = torch.zeros(pages, H, D // 8, P, 8, dtype=torch.bfloat16, device=cuda)
+    vc = torch.zeros(pages, H, D, P, dtype=torch.bfloat16, device=cuda)
+    slots = torch.randperm(pages * P, generator=torch.Generator().manual_seed(3))[:T].to(cuda)
+    slots[7] = -1
+    b200decode.append_kv(key, val, kc, vc, slots, kv_layout="vllm")
+    torch.cuda.synchronize()
+    k_nhd = kc.permute(0, 3, 1, 2, 4).reshape(pages, P, H, D)
+    v_nhd = vc.permute(0, 3, 1, 2)
+    for got, src in ((k_nhd, key), (v_nhd, val)):
+        ref = np.zeros((pages, P, H, D))
+        R.append_kv(ref, to_oracle(src).astype(np.float32), slots.cpu().numpy(), P)
+        np.testing.assert_array_equal(to_oracle(got.contiguous()), ref)
+    # decode one sequence over every written slot, in slot order
+    used = torch.sort(slots[slots >= 0]).values
+    L = int(used.numel())
+    bt_pages = torch.unique(used // P)
+    assert bt_pages.numel() <= pages
+    # a sequence whose pages are all pages (identity), length = pages * P,
+    # with unwritten slots zero: decode both layouts and compare
+    q = torch.randn(1, 4 * H, D, generator=g, device=cuda).to(torch.bfloat16)
+    bt = torch.arange(pages, dtype=torch.int32, device=cuda)[None]
+    sl = torch.tensor([pages * P], dtype=torch.int32, device=cuda)
+    o1, l1 = b200decode.decode(q, kc, vc, sl, bt, kv_layout="vllm")
+    o2, l2 = b200decode.decode(q, k_nhd.contiguous(), v_nhd.contiguous(), sl, bt)
+    torch.cuda.synchronize()
+    assert L == T - 1
+    torch.testing.assert_close(o1.float(), o2.float(), atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(l1, l2, atol=1e-3, rtol=0)
