@@ -76,17 +76,7 @@ extern "C" int b2d_decode_mla(const b2d_mla_args* a, void* stream) {
   if (!a->workspace || a->workspace_bytes < pl.ws_bytes) return B2D_ERR_WORKSPACE;
   if ((uintptr_t)a->workspace & 255) return B2D_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Q: {64 elems, head, 128-byte column block, sequence, 1}; box = 64 heads.
-  CUtensorMap tq, tkv;
-  {
-    const uint64_t dims[5] = {64, (uint64_t)a->num_heads, 9, (uint64_t)a->batch, 1};
-    const uint64_t strides[4] = {(uint64_t)a->q_stride_h * 2, 128, (uint64_t)a->q_stride_b * 2,
-                                 (uint64_t)a->q_stride_b * 2 * (uint64_t)a->batch};
-    const uint32_t box[5] = {64, 64, 9, 1, 1};
-    if (encode_tiled_map(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT16, 5, a->q, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_128B))
-      return B2D_ERR_CUDA;
-  }
+  CUtensorMap tkv;
   {
     const uint64_t dims[5] = {64, (uint64_t)a->page_size, 9, (uint64_t)a->num_pages, 1};
     const uint64_t strides[4] = {(uint64_t)a->kv_stride_tok * 2, 128,
@@ -104,6 +94,9 @@ extern "C" int b2d_decode_mla(const b2d_mla_args* a, void* stream) {
   for (int b0 = 0; b0 < a->batch; b0 += pl.seqs_per_launch) {
     const int nb = (a->batch - b0) < pl.seqs_per_launch ? (a->batch - b0) : pl.seqs_per_launch;
     MlaParams p{};
+    p.q = static_cast<const uint8_t*>(a->q) + (size_t)b0 * a->q_stride_b * 2;
+    p.q_sb = a->q_stride_b;
+    p.q_sh = a->q_stride_h;
     p.seqlens = a->cache_seqlens + b0;
     p.block_table = a->block_table + (size_t)b0 * a->block_table_stride;
     p.bt_stride = a->block_table_stride;
@@ -121,20 +114,8 @@ extern "C" int b2d_decode_mla(const b2d_mla_args* a, void* stream) {
     p.num_pages = (int)a->num_pages;
     p.max_pages = a->max_pages_per_seq;
     p.scale_log2 = a->softmax_scale * kLog2e;
-    // A batch slice's q rows start at sequence b0 of the Q tensor map.
-    CUtensorMap tq_slice = tq;
-    if (b0 > 0) {
-      const uint64_t dims[5] = {64, (uint64_t)a->num_heads, 9, (uint64_t)nb, 1};
-      const uint64_t strides[4] = {(uint64_t)a->q_stride_h * 2, 128, (uint64_t)a->q_stride_b * 2,
-                                   (uint64_t)a->q_stride_b * 2 * (uint64_t)nb};
-      const uint32_t box[5] = {64, 64, 9, 1, 1};
-      if (encode_tiled_map(&tq_slice, CU_TENSOR_MAP_DATA_TYPE_UINT16, 5,
-                           static_cast<const uint8_t*>(a->q) + (size_t)b0 * a->q_stride_b * 2,
-                           dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
-        return B2D_ERR_CUDA;
-    }
     if (!(a->flags & B2D_FLAG_COMBINE_ONLY)) {
-      kern<<<2 * pl.nr, mla::kThreads, pl.smem, st>>>(tq_slice, tkv, p);
+      kern<<<2 * pl.nr, mla::kThreads, pl.smem, st>>>(tkv, p);
       if (cudaGetLastError() != cudaSuccess) return B2D_ERR_CUDA;
     }
     if (!(a->flags & B2D_FLAG_SKIP_COMBINE)) {

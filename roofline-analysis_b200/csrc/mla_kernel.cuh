@@ -10,28 +10,30 @@
 // 64 query heads [64h, 64h+64) of range r.  Both CTAs of a pair stream the
 // same KV tiles close together in time, so the second read is an L2 hit.
 //
-// Tensor memory (512 columns x 128 lanes, fp32): an M=64 UMMA writes its 64
-// rows to 16 lanes of each 32-lane quadrant, lane half 0 (lanes 0-15,
-// 32-47, ...) or lane half 1 (16-31, ...) as the address selects.  The O
-// accumulator [64 heads x 512] takes columns 0-255 of both halves (half 0:
-// dims 0-255, half 1: dims 256-511); the score tiles S [64 heads x 64 tokens]
-// (double-buffered) take columns 256-383 of half 0.  Thread i of softmax
-// warp w owns head 16w + (i & 15): lanes < 16 read its S row (one whole row
-// per thread: row max and sum need no shuffles) and hold O dims 0-255, lanes
-// >= 16 hold O dims 256-511.  Rescaling O rewrites columns 0-255 only, so it
-// never touches a score tile the tensor core may be writing.
+// Tensor memory (512 columns x 128 lanes).  An M=64 UMMA uses 16 lanes of
+// each 32-lane quadrant: lane half 0 (lanes 0-15, 32-47, ...) or lane half 1
+// (16-31, ...).  Half 0 holds the two score tiles S [64 heads x 64 tokens]
+// (columns 0-127) and the query Q [64 heads x 576] as packed bf16 pairs
+// (columns 128-415): S = Q.K^T reads Q straight from tensor memory (an
+// A-from-TMEM MMA, whose A must sit in the accumulator's lane half), so Q is
+// not re-read from shared memory for every chunk.  Half 1 holds the output
+// accumulator O [64 heads x 512] fp32 (columns 0-511).  Thread i of softmax
+// warp w serves head 16w + (i & 15): lanes < 16 own that head's S row (one
+// whole row per thread: no shuffles for max and sum); O, Q and rescaling go
+// through 16-lane tcgen05.ld/st, which touch one lane half only.
 //
-// Shared memory: Q [9 x 64 heads x 64] and each KV stage [9 x 32 tok x 64]
-// bf16 arrive by TMA with 128-byte swizzle (K-major canonical UMMA layout:
-// 8-row x 128-byte atoms, 1024-byte stride).  The same KV stage is the
-// K-major B operand of S = Q.K^T and the MN-major B operand of O += P.V
-// (V = its first 8 column blocks), so each latent row is fetched once.
-// P goes to shared memory as bf16 in the same swizzled K-major layout.
+// Shared memory: three KV stages [9 x 64 tok x 64] bf16 by TMA with 128-byte
+// swizzle (K-major canonical UMMA layout: 8-row x 128-byte atoms, 1024-byte
+// stride), and P [64 heads x 64 tok] bf16 in the same layout.  The same KV
+// stage is the K-major B operand of S = Q.K^T and the MN-major B operand of
+// O += P.V (V = its first 8 column blocks), so each latent row is fetched
+// once.
 //
-// Warp roles: warps 0-3 softmax + epilogue, warp 4 TMA producer, warp 5
-// TMEM allocator + single-thread MMA issuer.  Online softmax uses a lazy
-// rescale: the running max moves only when a score exceeds it by 8 (log2
-// units), so P <= 256 fits bf16 and O is rescaled (TMEM round trip) rarely.
+// Warp roles: warps 0-3 softmax + epilogue (and the Q writes), warp 4 TMA
+// producer, warp 5 TMEM allocator + single-thread MMA issuer.  Online softmax
+// uses a lazy rescale: the running max moves only when a score exceeds it by
+// 8 (log2 units), so P <= 256 fits bf16 and O is rescaled (TMEM round trip)
+// rarely.
 #pragma once
 
 #include "gqa_kernel.cuh"
@@ -40,6 +42,8 @@
 namespace b2d {
 
 struct MlaParams {
+  const void* q;             // bf16 [B, 128, 576] (strides in elements)
+  int64_t q_sb, q_sh;
   const int32_t* seqlens;
   const int32_t* block_table;
   int64_t bt_stride;
@@ -60,14 +64,12 @@ constexpr int kHeads = 64;         // query heads per CTA
 constexpr int kDqk = 576, kDv = 512;
 constexpr int kCB = kDqk / 64;     // 128-byte column blocks per row (9)
 constexpr int kT = 64;             // tokens per chunk (one TMA box; page size % 64 == 0)
-constexpr int kStages = 2;
-constexpr uint32_t kQBytes = kCB * kHeads * 128;     // 73728
+constexpr int kStages = 3;
 constexpr uint32_t kStageBytes = kCB * kT * 128;     // 73728
-constexpr int kSplit = 1;          // independent QK accumulators per score tile
-constexpr int kSBuf = 2;           // score tiles in TMEM (lane half 0, columns 256 + 64k)
-constexpr int kPBuf = 1;           // P tile in shared memory (64 heads x 64 tokens bf16)
+constexpr int kSBuf = 2;           // score tiles in TMEM (lane half 0, columns 64k)
 constexpr uint32_t kPBytes = kHeads * 128;           // 8192
-constexpr int kAhead = 1;          // QK tiles issued ahead of the oldest pending P.V
+constexpr uint32_t kColQ = kSBuf * kT;               // Q: lane half 0, columns 128-415
+constexpr uint32_t kHalf1 = 16u << 16;               // TMEM lane offset of lane half 1 (O)
 constexpr float kLazy = 8.f;                         // lazy-rescale threshold, log2 units
 #ifndef B2D_MLA_L2_AHEAD
 #define B2D_MLA_L2_AHEAD 2
@@ -75,12 +77,11 @@ constexpr float kLazy = 8.f;                         // lazy-rescale threshold, 
 constexpr int kL2Ahead = B2D_MLA_L2_AHEAD;           // chunks prefetched into L2 past the ring
 constexpr int kThreads = 6 * 32;
 // shared-memory map (offsets from the 1024-aligned base)
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffKV = kOffQ + kQBytes;
+constexpr uint32_t kOffKV = 0;
 constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;
-constexpr uint32_t kOffBar = kOffP + kPBuf * kPBytes;
-// kv full/empty, q full/empty, s full, p full, pv done, o full/empty
-constexpr uint32_t kNumBars = 2 * kStages + 2 + kSBuf + kPBuf + kPBuf + 2;
+constexpr uint32_t kOffBar = kOffP + kPBytes;
+// kv full/empty, q full, s full, p full, pv done, o full/empty
+constexpr uint32_t kNumBars = 2 * kStages + 1 + kSBuf + 2 + 2;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffRows = kOffTmem + 16;
 }  // namespace mla
@@ -214,9 +215,63 @@ __device__ __forceinline__ bool mla_wait(uint64_t* bar, uint32_t parity, int* st
   return false;
 }
 
+
+// A-from-TMEM MMA: D (TMEM) (+)= A (TMEM, K-major, packed 16-bit pairs) .
+// B (shared-memory descriptor).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                             uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate), "r"(0u),
+      "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
+// 16-lane tensor-memory access, 8 column groups of 8 columns (16x256b.x8):
+// register 4j + e of thread t is lane (t / 4) + 8 (e >> 1), column
+// 8j + 2 (t % 4) + (e & 1), counted from the address's lane and column.
+__device__ __forceinline__ void tmem_ld16x8(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st16x8(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x256b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 16-lane store of 4 column groups (16x256b.x4), same register mapping.
+__device__ __forceinline__ void tmem_st16x4(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 __global__ void __launch_bounds__(mla::kThreads, 1)
-    mla_decode_kernel(const __grid_constant__ CUtensorMap tmap_q,
-                      const __grid_constant__ CUtensorMap tmap_kv, const MlaParams p) {
+    mla_decode_kernel(const __grid_constant__ CUtensorMap tmap_kv, const MlaParams p) {
   using namespace mla;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -224,12 +279,11 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + kStages;
-  uint64_t* q_full = bars + 2 * kStages;
-  uint64_t* q_empty = q_full + 1;
-  uint64_t* s_full = q_full + 2;      // [kSBuf]
-  uint64_t* p_full = s_full + kSBuf;  // [kPBuf]
-  uint64_t* pv_done = p_full + kPBuf; // [kPBuf]
-  uint64_t* o_full = pv_done + kPBuf;
+  uint64_t* q_full = bars + 2 * kStages;   // Q of the next sequence written to TMEM
+  uint64_t* s_full = q_full + 1;          // [kSBuf]
+  uint64_t* p_full = s_full + kSBuf;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* o_full = pv_done + 1;
   uint64_t* o_empty = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
   int32_t* row_start = reinterpret_cast<int32_t*>(smem + kOffRows);
@@ -246,13 +300,10 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
       mbar_init(kv_full + s, 1);
       mbar_init(kv_empty + s, 1);
     }
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    mbar_init(q_full, 128);
     for (int j = 0; j < kSBuf; ++j) mbar_init(s_full + j, 1);
-    for (int j = 0; j < kPBuf; ++j) {
-      mbar_init(p_full + j, 128);
-      mbar_init(pv_done + j, 1);
-    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
     mbar_init(o_full, 1);
     mbar_init(o_empty, 128);
     fence_barrier_init();
@@ -263,10 +314,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (warp == 4 && lane == 0) {
-    prefetch_tmap(&tmap_q);
-    prefetch_tmap(&tmap_kv);
-  }
+  if (warp == 4 && lane == 0) prefetch_tmap(&tmap_kv);
   // Row table (chunks of kT tokens per sequence); reuses the GQA scan.
   {
     GqaParams gp{};
@@ -290,21 +338,14 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
   const int cap = p.max_pages * p.P;
 
   if (warp == 4) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (KV stages only) ----------------
     if (lane == 0 && active) {
       const uint64_t policy = kv_policy();
       int row = find_row(row_start, R, x0);
-      int cur = -1, nq = 0, s = 0;
+      int s = 0;
       uint32_t ph = 0;
       for (int x = x0; x < x1; ++x) {
         while (x >= row_start[row + 1]) ++row;
-        if (row != cur) {
-          cur = row;
-          if (!mla_wait(q_empty, (nq & 1) ^ 1u, p.status)) break;
-          mbar_arrive_expect_tx(q_full, kQBytes);
-          tma_load_5d(smem + kOffQ, &tmap_q, q_full, kHeads * half, 0, row, 0, 0);
-          ++nq;
-        }
         const int tok0 = (x - row_start[row]) * kT;
         const int pidx = tok0 / p.P;
         int pg = __ldg(p.block_table + (int64_t)row * p.bt_stride + pidx);
@@ -340,61 +381,44 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
     if (active) {
       const uint32_t idesc_qk = umma_idesc_bf16(64, kT, false);
       const uint32_t idesc_pv = umma_idesc_bf16(64, 256, true);
-      const uint32_t t_o = tmem;                          // O: cols 0..255, both lane halves
-      const uint32_t t_s = tmem + 256u;                   // S: lane half 0, cols 256..319
+      const uint32_t t_o = tmem + kHalf1;                 // O: lane half 1, columns 0..511
+      const uint32_t t_q = tmem + kColQ;                  // Q: lane half 0, columns 128..415
       int row = find_row(row_start, R, x0);
       int cur = -1, nq = 0, nrow = 0, s = 0;
       uint32_t ph = 0;
       bool ok = true;
       auto issue_pv = [&](int j, int stage, bool first_of_row) -> bool {
-        if (!mla_wait(p_full + j % kPBuf, (uint32_t)((j / kPBuf) & 1), p.status)) return false;
+        if (!mla_wait(p_full, (uint32_t)(j & 1), p.status)) return false;
         if (first_of_row && nrow > 1) {
           if (!mla_wait(o_empty, (uint32_t)((nrow - 2) & 1), p.status)) return false;
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t pa = sbase + kOffP + (uint32_t)((j % kPBuf) * kPBytes);
-          const uint32_t vb = sbase + kOffKV + stage * kStageBytes;
-          const uint64_t pd0 = umma_desc_sw128(pa, 16, 1024);
-          const uint64_t vd0 = umma_desc_sw128(vb, kT * 128, 1024);
+          const uint64_t pd0 = umma_desc_sw128(sbase + kOffP, 16, 1024);
+          const uint64_t vd0 = umma_desc_sw128(sbase + kOffKV + stage * kStageBytes, kT * 128, 1024);
 #pragma unroll
           for (int ks = 0; ks < kT / 16; ++ks) {
             const uint64_t ad = pd0 + (uint64_t)((ks * 32) >> 4);
 #pragma unroll
             for (int hv = 0; hv < 2; ++hv) {
               const uint64_t bd = vd0 + (uint64_t)((hv * 4 * (kT * 128) + ks * 16 * 128) >> 4);
-              umma_bf16(t_o + ((uint32_t)hv << 20), ad, bd, idesc_pv, !(first_of_row && ks == 0));
+              umma_bf16(t_o + (uint32_t)(hv * 256), ad, bd, idesc_pv, !(first_of_row && ks == 0));
             }
           }
           umma_commit(kv_empty + stage);
-          umma_commit(pv_done + j % kPBuf);
+          umma_commit(pv_done);
         }
         __syncwarp();
         return true;
       };
-      // Chunks whose QK is issued but whose P.V is not (a short FIFO): QK runs
-      // kAhead chunks ahead so the tensor pipe has work while the softmax
-      // warps turn S(i) into P(i).
-      int pend_i[kAhead + 1], pend_s[kAhead + 1];
-      bool pend_f[kAhead + 1];
-      int np = 0;
-      auto pop_pv = [&]() -> bool {
-        const bool r = issue_pv(pend_i[0], pend_s[0], pend_f[0]);
-        for (int k = 1; k < np; ++k) {
-          pend_i[k - 1] = pend_i[k];
-          pend_s[k - 1] = pend_s[k];
-          pend_f[k - 1] = pend_f[k];
-        }
-        --np;
-        return r;
-      };
+      // QK of chunk i is issued before P.V of chunk i - 1, so the tensor pipe
+      // has work while the softmax warps turn S(i - 1) into P(i - 1).
+      int pend_i = -1, pend_s = 0;
+      bool pend_f = false;
       auto drain_row = [&]() -> bool {
-        while (np > 0)
-          if (!pop_pv()) return false;
-        if (lane == 0) {
-          umma_commit(o_full);
-          umma_commit(q_empty);
-        }
+        if (pend_i >= 0 && !issue_pv(pend_i, pend_s, pend_f)) return false;
+        pend_i = -1;
+        if (lane == 0) umma_commit(o_full);
         __syncwarp();
         return true;
       };
@@ -412,28 +436,23 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         if (!mla_wait(kv_full + s, ph, p.status)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t kb = sbase + kOffKV + s * kStageBytes;
-          const uint32_t qb = sbase + kOffQ;
-          const uint32_t ts = t_s + (uint32_t)((i % kSBuf) * kSplit * kT);
-          // Descriptors differ from the tile bases only in the start-address
-          // field (16-byte units), so each k-step adds a constant.
-          const uint64_t ad0 = umma_desc_sw128(qb, 16, 1024);
-          const uint64_t bd0 = umma_desc_sw128(kb, 16, 1024);
+          const uint32_t ts = tmem + (uint32_t)((i % kSBuf) * kT);
+          // The K descriptor differs from the tile base only in its start
+          // address (16-byte units); Q's k-step is 8 TMEM columns (16 bf16).
+          const uint64_t bd0 = umma_desc_sw128(sbase + kOffKV + s * kStageBytes, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < kDqk / 16; ++kk) {
             const int cb = kk >> 2, ko = (kk & 3) * 32;
-            const uint64_t ad = ad0 + (uint64_t)((cb * (kHeads * 128) + ko) >> 4);
             const uint64_t bd = bd0 + (uint64_t)((cb * (kT * 128) + ko) >> 4);
-            umma_bf16(ts + (uint32_t)((kk % kSplit) * kT), ad, bd, idesc_qk, kk >= kSplit);
+            umma_bf16_ts(ts, t_q + (uint32_t)(kk * 8), bd, idesc_qk, kk > 0);
           }
           umma_commit(s_full + i % kSBuf);
         }
         __syncwarp();
-        pend_i[np] = i;
-        pend_s[np] = s;
-        pend_f[np] = first;
-        ++np;
-        while (np > kAhead && ok) ok = pop_pv();
+        if (pend_i >= 0 && !(ok = issue_pv(pend_i, pend_s, pend_f))) break;
+        pend_i = i;
+        pend_s = s;
+        pend_f = first;
         if (++s == kStages) {
           s = 0;
           ph ^= 1u;
@@ -445,10 +464,41 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
     // ---------------- softmax + epilogue (warps 0-3) ----------------
     if (active) {
       const int hr = 16 * warp + (lane & 15);         // head row within this CTA
-      const bool s_lane = lane < 16;                  // holds the S row and O dims 0-255
+      const bool s_lane = lane < 16;                  // holds the S row of head hr
       const uint32_t t_warp = tmem + ((uint32_t)(32 * warp) << 16);
+      // 16-lane O / Q accesses: this thread's two heads (lanes t/4, t/4 + 8 of
+      // the warp's lane half) and columns 2 (t % 4) + {0, 1} of every group of 8.
+      const int h_a = 16 * warp + (lane >> 2), h_b = h_a + 8;
+      const int cq = 2 * (lane & 3);
       constexpr float kLn2 = 0.69314718055994530942f;
+      // Q of a sequence into TMEM (lane half 0, columns 128..415, bf16 pairs
+      // with the lower dim in the low half), then release it to the MMA warp.
+      auto write_q = [&](int qrow) {
+        const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(p.q) +
+                                  (int64_t)qrow * p.q_sb;
+        const __nv_bfloat16* qa = qb + (int64_t)(kHeads * half + h_a) * p.q_sh;
+        const __nv_bfloat16* qc = qb + (int64_t)(kHeads * half + h_b) * p.q_sh;
+#pragma unroll 1
+        for (int g0 = 0; g0 < kDqk / 16; g0 += 4) {   // 4 groups of 16 dims per store
+          uint32_t r[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int d = 16 * (g0 + j) + 2 * cq;
+            const uint2 va = *reinterpret_cast<const uint2*>(qa + d);
+            const uint2 vc = *reinterpret_cast<const uint2*>(qc + d);
+            r[4 * j + 0] = va.x;
+            r[4 * j + 1] = va.y;
+            r[4 * j + 2] = vc.x;
+            r[4 * j + 3] = vc.y;
+          }
+          tmem_st16x4(t_warp + kColQ + (uint32_t)(8 * g0), r);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive(q_full);
+      };
       int row = find_row(row_start, R, x0);
+      write_q(row);
       int cur = -1, nrow = 0, L = 0;
       float m = -INFINITY, l = 0.f;
       bool ok = true;
@@ -474,15 +524,8 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         float sv[kT];
 #pragma unroll
         for (int c = 0; c < kT; c += 32)
-          tmem_ld32(t_warp + 256u + (uint32_t)((i % kSBuf) * kSplit * kT + c), sv + c);
-#pragma unroll
-        for (int part = 1; part < kSplit; ++part) {
-          float sp[kT];
-          tmem_ld32(t_warp + 256u + (uint32_t)(((i % kSBuf) * kSplit + part) * kT), sp);
-#pragma unroll
-          for (int t = 0; t < kT; ++t) sv[t] += sp[t];
-        }
-        // Lanes >= 16 read unused columns of lane half 1 here; lanes < 16 hold the S row.
+          tmem_ld32(t_warp + (uint32_t)((i % kSBuf) * kT + c), sv + c);
+        // Lanes >= 16 read O columns of lane half 1 here and ignore them.
         float cm = -INFINITY;
 #pragma unroll
         for (int t = 0; t < kT; ++t) {
@@ -498,29 +541,31 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           m = mn;
           l *= alpha;
         }
-        // both O threads of this head use the S-row thread's factor
-        const float alpha_o = __shfl_sync(0xffffffffu, alpha, lane & 15);
-        if (any_need && !first_chunk) {
-          // O must be complete up to the previous chunk before it is rescaled.
-          if (!mla_wait(pv_done + (i - 1) % kPBuf, (uint32_t)(((i - 1) / kPBuf) & 1), p.status)) { ok = false; break; }
+        // P.V of the previous chunk must be complete before O is rescaled or
+        // the P tile is rewritten.
+        if (i > 0) {
+          if (!mla_wait(pv_done, (uint32_t)((i - 1) & 1), p.status)) { ok = false; break; }
           tc_fence_after();
-          for (int c = 0; c < kDv / 2; c += 32) {
-            float ov[32];
-            tmem_ld32(t_warp + (uint32_t)c, ov);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] *= alpha_o;
-            tmem_st32(t_warp + (uint32_t)c, ov);
-          }
-          tc_fence_before();
         }
-        // P(i - kPBuf) must be consumed before its TMEM buffer is rewritten.
-        if (i >= kPBuf) {
-          if (!mla_wait(pv_done + i % kPBuf, (uint32_t)(((i - kPBuf) / kPBuf) & 1), p.status)) { ok = false; break; }
+        if (any_need && !first_chunk) {
+          const float al_a = __shfl_sync(0xffffffffu, alpha, lane >> 2);
+          const float al_b = __shfl_sync(0xffffffffu, alpha, (lane >> 2) + 8);
+          for (int c = 0; c < kDv; c += 64) {
+            uint32_t r[32];
+            tmem_ld16x8(t_warp + kHalf1 + (uint32_t)c, r);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              r[4 * j + 0] = __float_as_uint(__uint_as_float(r[4 * j + 0]) * al_a);
+              r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) * al_a);
+              r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) * al_b);
+              r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) * al_b);
+            }
+            tmem_st16x8(t_warp + kHalf1 + (uint32_t)c, r);
+          }
         }
         if (s_lane) {
           // P row (bf16) into the swizzled K-major P tile: row hr is 128-byte
           // line hr, its 16-byte chunk c (8 tokens) sits at c ^ (hr & 7).
-          uint8_t* pbuf = smem + kOffP + (i % kPBuf) * kPBytes;
           float psum = 0.f;
           uint32_t pk[kT / 2];
 #pragma unroll
@@ -532,7 +577,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           l += psum;
 #pragma unroll
           for (int c = 0; c < kT / 8; ++c) {
-            const uint32_t a = smem_u32(pbuf) + hr * 128 + (((c ^ (hr & 7)) & 7) << 4);
+            const uint32_t a = sbase + kOffP + hr * 128 + (((c ^ (hr & 7)) & 7) << 4);
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(pk[4 * c]),
                          "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
                          : "memory");
@@ -552,46 +597,51 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         }
         fence_async_smem();
         tc_fence_before();
-        mbar_arrive(p_full + i % kPBuf);
+        mbar_arrive(p_full);
 
         if (last) {
+          // S of this row's last chunk has been read, so its QK MMAs are done
+          // and the Q columns are free: stage the next sequence's Q now.
+          if (x + 1 < x1) write_q(row + 1);
           if (!mla_wait(o_full, (uint32_t)((nrow - 1) & 1), p.status)) { ok = false; break; }
           tc_fence_after();
-          const float l_o = __shfl_sync(0xffffffffu, l, lane & 15);
-          const float m_o = __shfl_sync(0xffffffffu, m, lane & 15);
           const int cf = cta_of_chunk(row_start[row], W, G);
           const int cl = cta_of_chunk(row_start[row + 1] - 1, W, G);
-          const int head = kHeads * half + hr;
-          const float inv = 1.f / l_o;
-          const int dv0 = s_lane ? 0 : kDv / 2;   // this thread's half of the head dims
-          for (int c = 0; c < kDv / 2; c += 32) {
-            float ov[32];
-            tmem_ld32(t_warp + (uint32_t)c, ov);
-            {
-              if (cf == cl) {
-                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) +
-                                     (int64_t)row * p.o_sb + (int64_t)head * p.o_sh + dv0 + c;
+          const float l_a = __shfl_sync(0xffffffffu, l, lane >> 2);
+          const float l_b = __shfl_sync(0xffffffffu, l, (lane >> 2) + 8);
+          const float inv_a = 1.f / l_a, inv_b = 1.f / l_b;
+          const int head_a = kHeads * half + h_a, head_b = kHeads * half + h_b;
+          for (int c = 0; c < kDv; c += 64) {
+            uint32_t r[32];
+            tmem_ld16x8(t_warp + kHalf1 + (uint32_t)c, r);
+            if (cf == cl) {
+              __nv_bfloat16* da = reinterpret_cast<__nv_bfloat16*>(p.out) +
+                                  (int64_t)row * p.o_sb + (int64_t)head_a * p.o_sh + c + cq;
+              __nv_bfloat16* db = reinterpret_cast<__nv_bfloat16*>(p.out) +
+                                  (int64_t)row * p.o_sb + (int64_t)head_b * p.o_sh + c + cq;
 #pragma unroll
-                for (int e = 0; e < 32; e += 8) {
-                  uint4 w;
-                  w.x = pack2<true>(ov[e] * inv, ov[e + 1] * inv);
-                  w.y = pack2<true>(ov[e + 2] * inv, ov[e + 3] * inv);
-                  w.z = pack2<true>(ov[e + 4] * inv, ov[e + 5] * inv);
-                  w.w = pack2<true>(ov[e + 6] * inv, ov[e + 7] * inv);
-                  *reinterpret_cast<uint4*>(dst + e) = w;
-                }
-              } else {
-                const int64_t seg = (int64_t)row + range;
-                float* dst = p.part_o + (seg * 128 + head) * kDv + dv0 + c;
+              for (int j = 0; j < 8; ++j) {
+                *reinterpret_cast<uint32_t*>(da + 8 * j) =
+                    pack2<true>(__uint_as_float(r[4 * j]) * inv_a, __uint_as_float(r[4 * j + 1]) * inv_a);
+                *reinterpret_cast<uint32_t*>(db + 8 * j) =
+                    pack2<true>(__uint_as_float(r[4 * j + 2]) * inv_b, __uint_as_float(r[4 * j + 3]) * inv_b);
+              }
+            } else {
+              const int64_t seg = (int64_t)row + range;
+              float* da = p.part_o + (seg * 128 + head_a) * kDv + c + cq;
+              float* db = p.part_o + (seg * 128 + head_b) * kDv + c + cq;
 #pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                  *reinterpret_cast<float4*>(dst + e) =
-                      make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
+              for (int j = 0; j < 8; ++j) {
+                *reinterpret_cast<float2*>(da + 8 * j) =
+                    make_float2(__uint_as_float(r[4 * j]) * inv_a, __uint_as_float(r[4 * j + 1]) * inv_a);
+                *reinterpret_cast<float2*>(db + 8 * j) =
+                    make_float2(__uint_as_float(r[4 * j + 2]) * inv_b, __uint_as_float(r[4 * j + 3]) * inv_b);
               }
             }
           }
           if (s_lane) {
-            const float lse2 = m_o + fast_log2(l_o);
+            const int head = kHeads * half + hr;
+            const float lse2 = m + fast_log2(l);
             if (cf == cl) {
               if (p.lse) p.lse[(int64_t)row * p.lse_sb + head] = lse2 * kLn2;
             } else {
