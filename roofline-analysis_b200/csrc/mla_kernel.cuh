@@ -17,10 +17,12 @@
 // (columns 128-415): S = Q.K^T reads Q straight from tensor memory (an
 // A-from-TMEM MMA, whose A must sit in the accumulator's lane half), so Q is
 // not re-read from shared memory for every chunk.  Half 1 holds the output
-// accumulator O [64 heads x 512] fp32 (columns 0-511).  Thread i of softmax
-// warp w serves head 16w + (i & 15): lanes < 16 own that head's S row (one
-// whole row per thread: no shuffles for max and sum); O, Q and rescaling go
-// through 16-lane tcgen05.ld/st, which touch one lane half only.
+// accumulator O [64 heads x 512] fp32 (columns 0-511).  All tensor-memory
+// traffic of the softmax warps uses the 16-lane 16x256b shape, which touches
+// one lane half only: thread t of warp w serves heads 16w + t/4 and
+// 16w + t/4 + 8, columns 2 (t % 4) + {0, 1} of every group of 8 (16 scores
+// per head per chunk; the 4 threads of a head combine max and sum with two
+// shuffles).
 //
 // Shared memory: three KV stages [9 x 64 tok x 64] bf16 by TMA with 128-byte
 // swizzle (K-major canonical UMMA layout: 8-row x 128-byte atoms, 1024-byte
@@ -151,44 +153,6 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// 32 consecutive fp32 TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
-      "%29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
-      "%29, %30, %31, %32};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-      : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Named barrier over the 128 softmax threads; returns whether any thread's
@@ -463,8 +427,6 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
   } else {
     // ---------------- softmax + epilogue (warps 0-3) ----------------
     if (active) {
-      const int hr = 16 * warp + (lane & 15);         // head row within this CTA
-      const bool s_lane = lane < 16;                  // holds the S row of head hr
       const uint32_t t_warp = tmem + ((uint32_t)(32 * warp) << 16);
       // 16-lane O / Q accesses: this thread's two heads (lanes t/4, t/4 + 8 of
       // the warp's lane half) and columns 2 (t % 4) + {0, 1} of every group of 8.
@@ -500,7 +462,9 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
       int row = find_row(row_start, R, x0);
       write_q(row);
       int cur = -1, nrow = 0, L = 0;
-      float m = -INFINITY, l = 0.f;
+      // running max (log2 units) and partial sum of this thread's two heads;
+      // the 4 threads of a head hold the same max and disjoint partial sums
+      float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
       bool ok = true;
       int i = 0;
       for (int x = x0; x < x1 && ok; ++x, ++i) {
@@ -510,8 +474,8 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           ++nrow;
           const int Lb = __ldg(p.seqlens + row);
           L = Lb < 0 ? 0 : (Lb > cap ? cap : Lb);
-          m = -INFINITY;
-          l = 0.f;
+          m_a = m_b = -INFINITY;
+          l_a = l_b = 0.f;
         }
         const bool first_chunk = (x == row_start[row]) || (x == x0);
         const bool last = (x + 1 == x1) || (x + 1 >= row_start[row + 1]);
@@ -521,25 +485,47 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
 
         if (!mla_wait(s_full + i % kSBuf, (uint32_t)((i / kSBuf) & 1), p.status)) { ok = false; break; }
         tc_fence_after();
-        float sv[kT];
+        // Scores of heads a and b, tokens 8j + cq + {0, 1} (j = 0..7).
+        float sa[16], sb[16];
+        {
+          uint32_t r[32];
+          tmem_ld16x8(t_warp + (uint32_t)((i % kSBuf) * kT), r);
 #pragma unroll
-        for (int c = 0; c < kT; c += 32)
-          tmem_ld32(t_warp + (uint32_t)((i % kSBuf) * kT + c), sv + c);
-        // Lanes >= 16 read O columns of lane half 1 here and ignore them.
-        float cm = -INFINITY;
+          for (int j = 0; j < 8; ++j) {
 #pragma unroll
-        for (int t = 0; t < kT; ++t) {
-          sv[t] = (t < nvalid) ? sv[t] * p.scale_log2 : -INFINITY;
-          cm = fmaxf(cm, sv[t]);
+            for (int e = 0; e < 2; ++e) {
+              const bool valid = 8 * j + cq + e < nvalid;
+              sa[2 * j + e] = valid ? __uint_as_float(r[4 * j + e]) * p.scale_log2 : -INFINITY;
+              sb[2 * j + e] = valid ? __uint_as_float(r[4 * j + 2 + e]) * p.scale_log2 : -INFINITY;
+            }
+          }
         }
-        const bool need = s_lane && (m == -INFINITY || cm > m + kLazy);
-        const bool any_need = softmax_group_any(need);
-        float alpha = 1.f;
-        if (need) {
-          const float mn = (m == -INFINITY) ? cm : fmaxf(m, cm);
-          alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - mn);
-          m = mn;
-          l *= alpha;
+        float cm_a = -INFINITY, cm_b = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          cm_a = fmaxf(cm_a, sa[t]);
+          cm_b = fmaxf(cm_b, sb[t]);
+        }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+          cm_a = fmaxf(cm_a, __shfl_xor_sync(0xffffffffu, cm_a, o));
+          cm_b = fmaxf(cm_b, __shfl_xor_sync(0xffffffffu, cm_b, o));
+        }
+        const bool need_a = m_a == -INFINITY || cm_a > m_a + kLazy;
+        const bool need_b = m_b == -INFINITY || cm_b > m_b + kLazy;
+        const bool any_need = softmax_group_any(need_a || need_b);
+        float al_a = 1.f, al_b = 1.f;
+        if (need_a) {
+          const float mn = (m_a == -INFINITY) ? cm_a : fmaxf(m_a, cm_a);
+          al_a = (m_a == -INFINITY) ? 0.f : fast_exp2(m_a - mn);
+          m_a = mn;
+          l_a *= al_a;
+        }
+        if (need_b) {
+          const float mn = (m_b == -INFINITY) ? cm_b : fmaxf(m_b, cm_b);
+          al_b = (m_b == -INFINITY) ? 0.f : fast_exp2(m_b - mn);
+          m_b = mn;
+          l_b *= al_b;
         }
         // P.V of the previous chunk must be complete before O is rescaled or
         // the P tile is rewritten.
@@ -548,8 +534,6 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           tc_fence_after();
         }
         if (any_need && !first_chunk) {
-          const float al_a = __shfl_sync(0xffffffffu, alpha, lane >> 2);
-          const float al_b = __shfl_sync(0xffffffffu, alpha, (lane >> 2) + 8);
           for (int c = 0; c < kDv; c += 64) {
             uint32_t r[32];
             tmem_ld16x8(t_warp + kHalf1 + (uint32_t)c, r);
@@ -563,23 +547,23 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
             tmem_st16x8(t_warp + kHalf1 + (uint32_t)c, r);
           }
         }
-        if (s_lane) {
-          // P row (bf16) into the swizzled K-major P tile: row hr is 128-byte
-          // line hr, its 16-byte chunk c (8 tokens) sits at c ^ (hr & 7).
-          float psum = 0.f;
-          uint32_t pk[kT / 2];
+        {
+          // P (bf16) into the swizzled K-major P tile: head row h is 128-byte
+          // line h, tokens 8j..8j+7 are its 16-byte chunk j ^ (h & 7); this
+          // thread writes tokens 8j + cq, +1 of heads a and b.
+          const uint32_t pa = sbase + kOffP + (uint32_t)(h_a * 128 + 2 * cq);
+          const uint32_t pb = sbase + kOffP + (uint32_t)(h_b * 128 + 2 * cq);
 #pragma unroll
-          for (int t = 0; t < kT; t += 2) {
-            const float p0 = fast_exp2(sv[t] - m), p1 = fast_exp2(sv[t + 1] - m);
-            psum += p0 + p1;
-            pk[t / 2] = pack2<true>(p0, p1);
-          }
-          l += psum;
-#pragma unroll
-          for (int c = 0; c < kT / 8; ++c) {
-            const uint32_t a = sbase + kOffP + hr * 128 + (((c ^ (hr & 7)) & 7) << 4);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(pk[4 * c]),
-                         "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+          for (int j = 0; j < 8; ++j) {
+            const float a0 = fast_exp2(sa[2 * j] - m_a), a1 = fast_exp2(sa[2 * j + 1] - m_a);
+            const float b0 = fast_exp2(sb[2 * j] - m_b), b1 = fast_exp2(sb[2 * j + 1] - m_b);
+            l_a += a0 + a1;
+            l_b += b0 + b1;
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pa + (((j ^ (h_a & 7)) & 7) << 4)),
+                         "r"(pack2<true>(a0, a1))
+                         : "memory");
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pb + (((j ^ (h_b & 7)) & 7) << 4)),
+                         "r"(pack2<true>(b0, b1))
                          : "memory");
           }
         }
@@ -603,13 +587,17 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           // S of this row's last chunk has been read, so its QK MMAs are done
           // and the Q columns are free: stage the next sequence's Q now.
           if (x + 1 < x1) write_q(row + 1);
+          float lt_a = l_a, lt_b = l_b;
+#pragma unroll
+          for (int o = 1; o <= 2; o <<= 1) {
+            lt_a += __shfl_xor_sync(0xffffffffu, lt_a, o);
+            lt_b += __shfl_xor_sync(0xffffffffu, lt_b, o);
+          }
           if (!mla_wait(o_full, (uint32_t)((nrow - 1) & 1), p.status)) { ok = false; break; }
           tc_fence_after();
           const int cf = cta_of_chunk(row_start[row], W, G);
           const int cl = cta_of_chunk(row_start[row + 1] - 1, W, G);
-          const float l_a = __shfl_sync(0xffffffffu, l, lane >> 2);
-          const float l_b = __shfl_sync(0xffffffffu, l, (lane >> 2) + 8);
-          const float inv_a = 1.f / l_a, inv_b = 1.f / l_b;
+          const float inv_a = 1.f / lt_a, inv_b = 1.f / lt_b;
           const int head_a = kHeads * half + h_a, head_b = kHeads * half + h_b;
           for (int c = 0; c < kDv; c += 64) {
             uint32_t r[32];
@@ -639,13 +627,16 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
               }
             }
           }
-          if (s_lane) {
-            const int head = kHeads * half + hr;
-            const float lse2 = m + fast_log2(l);
+          if ((lane & 3) == 0) {
+            const float lse_a = m_a + fast_log2(lt_a), lse_b = m_b + fast_log2(lt_b);
             if (cf == cl) {
-              if (p.lse) p.lse[(int64_t)row * p.lse_sb + head] = lse2 * kLn2;
+              if (p.lse) {
+                p.lse[(int64_t)row * p.lse_sb + head_a] = lse_a * kLn2;
+                p.lse[(int64_t)row * p.lse_sb + head_b] = lse_b * kLn2;
+              }
             } else {
-              p.part_lse[((int64_t)row + range) * 128 + head] = lse2;
+              p.part_lse[((int64_t)row + range) * 128 + head_a] = lse_a;
+              p.part_lse[((int64_t)row + range) * 128 + head_b] = lse_b;
             }
           }
           tc_fence_before();
