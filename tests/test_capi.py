@@ -70,6 +70,24 @@ def test_workspace_query_and_plan_on_host():
                                 C.byref(hk)) == 0
 
 
+def test_tile_width_plan():
+    """KV heads per tile: whole token rows (8 heads) for 16-bit caches, 4 for
+    fp8, narrower when the block table bounds the problem to fewer chunks
+    than about two per CTA (host-only plan, no GPU)."""
+    lib = _lib.load()
+    nc, t, hk = C.c_int32(), C.c_int32(), C.c_int32()
+
+    def plan(**kw):
+        assert lib.b2d_gqa_plan(C.byref(_args(**kw)), C.byref(nc), C.byref(t), C.byref(hk)) == 0
+        return hk.value
+
+    assert plan() == 8                                      # B=64 x 8192 tokens, bf16
+    assert plan(kv_dtype=_lib.B2D_FP8_E4M3) == 4
+    small = plan(batch=1, max_pages_per_seq=256)            # B=1, 4096 tokens
+    assert small < 8 and 8 % small == 0
+    assert plan(batch=1, max_pages_per_seq=8192) == 8       # B=1, 128k tokens: plenty of chunks
+
+
 @pytest.mark.parametrize("kw,code", [
     (dict(head_dim=96), -2),                 # unsupported head_dim
     (dict(head_dim=192, kv_dtype=_lib.B2D_FP8_E4M3), -2),  # fp8 needs head_dim % 128 == 0

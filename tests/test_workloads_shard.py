@@ -102,3 +102,34 @@ def test_decodebench_shape_matches_reference_record():
     assert s.attention == "GQA" and s.kv_bytes == 64 * 4096 * 8 * 128 * 2 * 2
     assert DecodeShape(1, 10, 8, 8, 64, "fp8", 16).kv_bytes == 10 * 8 * 64 * 2
     assert DecodeShape(1, 10, 8, 1, 64, "fp16", 16).attention == "MQA"
+
+
+def test_to_vllm_layout_element_mapping():
+    """K [blocks, Hkv, D/x, P, x] (x = 16 bytes of elements), V [blocks, Hkv, D, P]
+    (decodebench/vllm_paged_kernel.py:102-123) hold the NHD cache's values."""
+    pages, P, H, D = 3, 16, 2, 64
+    k = torch.randn(pages, P, H, D).to(torch.bfloat16)
+    v = torch.randn(pages, P, H, D).to(torch.bfloat16)
+    kv, vv = W.to_vllm_layout(k, v)
+    x = 8
+    assert kv.shape == (pages, H, D // x, P, x) and vv.shape == (pages, H, D, P)
+    assert kv.is_contiguous() and vv.is_contiguous()
+    for (pg, t, h, d) in [(0, 0, 0, 0), (2, 15, 1, 63), (1, 7, 0, 9), (2, 3, 1, 40)]:
+        assert kv[pg, h, d // x, t, d % x] == k[pg, t, h, d]
+        assert vv[pg, h, d, t] == v[pg, t, h, d]
+
+
+def test_decodebench_mla_cli_defaults_match_reference_flags():
+    """`decodebench mla` takes trtllm_mla_benchmark.py's flags and defaults."""
+    from b200decode import decodebench
+    a = decodebench.parse_mla_args(["--batch-size", "2", "--context-len", "10",
+                                    "--num-q-heads", "128", "--kv-dtype", "bf16",
+                                    "--output", "x.json"])
+    assert (a.num_kv_heads, a.qk_nope_head_dim, a.kv_lora_rank, a.qk_rope_head_dim,
+            a.page_size, a.warmup_steps, a.repeat) == (1, 128, 512, 64, 64, 10, 50)
+    shape = decodebench.MlaDecodeShape(32, 32768, 128, 1, 128, 512, 64, "bf16", 64)
+    assert shape.head_dim_qk == 192 and shape.kv_bytes == 32 * 32768 * 576 * 2
+    g = decodebench.parse_args(["--batch-size", "1", "--context-len", "5", "--num-q-heads", "8",
+                                "--num-kv-heads", "8", "--head-dim", "128", "--kv-dtype", "bf16",
+                                "--page-size", "16", "--output", "y.json", "--kv-layout", "vllm"])
+    assert g.kv_layout == "vllm"
