@@ -215,6 +215,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--page-perm", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cuda-graph", action="store_true")
+    ap.add_argument("--kv-scale-range", type=float, nargs=2, default=None, metavar=("LO", "HI"),
+                    help="fp8 only: per-KV-head dequantisation scales ~ U[LO, HI] "
+                         "(default: unit scales, as the reference)")
     ap.add_argument("--kv-layout", default="NHD", choices=["NHD", "HND", "vllm"],
                     help="cache layout handed to the kernel (vllm = paged_attention's "
                          "K [blocks, Hkv, D/8, P, 8], V [blocks, Hkv, D, P])")
@@ -303,6 +306,8 @@ def main(argv=None) -> int:
     shape = DecodeShape(args.batch_size, args.context_len, args.num_q_heads, args.num_kv_heads,
                         args.head_dim, args.kv_dtype, args.page_size)
     kernel = B2DDecodeKernel(shape, args.seqlen_lo, args.seqlen_hi, args.page_perm, args.seed,
+                             kv_scale_range=(tuple(args.kv_scale_range) if args.kv_scale_range
+                                             else None),
                              use_graph=args.cuda_graph, kv_layout=args.kv_layout)
     for _ in range(args.warmup_steps):
         kernel.run()
@@ -346,6 +351,7 @@ def main(argv=None) -> int:
         "page_perm": args.page_perm,
         "cuda_graph": args.cuda_graph,
         "kv_layout": args.kv_layout,
+        "kv_scale_range": args.kv_scale_range,
     }
     args.output.parent.mkdir(parents=True, exist_ok=True)
     args.output.write_text(json.dumps(result, indent=2) + "\n", encoding="utf-8")
