@@ -168,10 +168,6 @@ __device__ __forceinline__ bool softmax_group_any(bool pred) {
   return r != 0;
 }
 
-__device__ __forceinline__ void softmax_group_sync() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-}
-
 // Wait helper that records a timeout; returns false when the kernel must stop.
 __device__ __forceinline__ bool mla_wait(uint64_t* bar, uint32_t parity, int* status) {
   if (mbar_wait(bar, parity)) return true;
