@@ -105,12 +105,12 @@ extern "C" int b2d_append_kv(const b2d_append_args* a, void* stream) {
     return B2D_ERR_UNSUPPORTED;
   if (a->src_dtype != B2D_BF16 && a->src_dtype != B2D_FP16) return B2D_ERR_UNSUPPORTED;
   if (a->cache_dtype != a->src_dtype && a->cache_dtype != B2D_FP8_E4M3) return B2D_ERR_UNSUPPORTED;
-  if (a->num_tokens == 0) return B2D_OK;
-  if (!a->key || !a->value || !a->k_cache || !a->v_cache || !a->slot_mapping || a->num_pages <= 0)
-    return B2D_ERR_INVALID_ARG;
   if (a->kv_layout != B2D_KV_STRIDED && a->kv_layout != B2D_KV_VLLM) return B2D_ERR_INVALID_ARG;
   const bool vllm = a->kv_layout == B2D_KV_VLLM;
   if (vllm && a->cache_dtype == B2D_FP8_E4M3) return B2D_ERR_UNSUPPORTED;
+  if (a->num_tokens == 0) return B2D_OK;
+  if (!a->key || !a->value || !a->k_cache || !a->v_cache || !a->slot_mapping || a->num_pages <= 0)
+    return B2D_ERR_INVALID_ARG;
   const int es = a->cache_dtype == B2D_FP8_E4M3 ? 1 : 2;
   if (((uintptr_t)a->key & 15) || ((uintptr_t)a->value & 15) || ((uintptr_t)a->k_cache & 15) ||
       ((uintptr_t)a->v_cache & 15))

@@ -131,3 +131,44 @@ def test_python_layer_refuses_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA"):
         b200decode.decode(q, kc, kc, torch.ones(1, dtype=torch.int32),
                           torch.zeros(1, 1, dtype=torch.int32))
+
+
+def _mla_args(**kw):
+    a = _lib.MlaArgs()
+    a.batch, a.num_heads, a.head_dim_qk, a.head_dim_v = 128, 128, 576, 512
+    a.page_size, a.max_pages_per_seq, a.dtype = 64, 256, _lib.B2D_BF16
+    a.num_ctas = 148
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_mla_workspace_and_validation_on_host():
+    """Workspace sizing and argument checks of the MLA entry points run on the
+    host (no GPU): partials for (rows + CTA pairs) segments x 128 heads x 512."""
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    assert lib.b2d_mla_workspace_bytes(C.byref(_mla_args()), C.byref(n)) == 0
+    assert n.value >= (128 + 74) * 128 * 512 * 4
+    for kw, code in ((dict(num_heads=64), -2), (dict(head_dim_qk=512), -2),
+                     (dict(dtype=_lib.B2D_FP16), -2), (dict(page_size=16), -2),
+                     (dict(page_size=0), -1), (dict(batch=-1), -1)):
+        assert lib.b2d_mla_workspace_bytes(C.byref(_mla_args(**kw)), C.byref(n)) == code, kw
+    assert lib.b2d_decode_mla(C.byref(_mla_args()), None) == -1      # null pointers
+    assert lib.b2d_decode_mla(C.byref(_mla_args(batch=0)), None) == 0  # nothing to do
+
+
+def test_append_validation_on_host():
+    lib = _lib.load()
+    a = _lib.AppendArgs()
+    a.num_tokens, a.num_kv_heads, a.head_dim, a.page_size = 4, 8, 128, 16
+    a.src_dtype, a.cache_dtype = _lib.B2D_BF16, _lib.B2D_BF16
+    assert lib.b2d_append_kv(C.byref(a), None) == -1                  # null pointers
+    a.head_dim = 96
+    assert lib.b2d_append_kv(C.byref(a), None) == -2                  # head_dim not built
+    a.head_dim, a.cache_dtype = 128, _lib.B2D_FP16
+    assert lib.b2d_append_kv(C.byref(a), None) == -2                  # cache must match or be fp8
+    a.cache_dtype, a.kv_layout = _lib.B2D_FP8_E4M3, _lib.B2D_KV_VLLM
+    assert lib.b2d_append_kv(C.byref(a), None) == -2                  # vLLM layout: 16-bit only
+    a.kv_layout, a.num_tokens = _lib.B2D_KV_STRIDED, 0
+    assert lib.b2d_append_kv(C.byref(a), None) == 0                   # nothing to append
