@@ -71,9 +71,9 @@ def e4m3_bits_to_f64(bits: np.ndarray) -> np.ndarray:
 
 
 def f64_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
-    """Round-to-nearest-even quantisation to e4m3fn with saturation at 448
-    (used to build FP8 test caches; matches torch's float8_e4m3fn cast for
-    finite inputs)."""
+    """Round-to-nearest-even quantisation to e4m3fn with saturation at 448;
+    the sign is kept, also when the result rounds to zero (-0 is 0x80), as
+    torch's float8_e4m3fn cast does for finite inputs within range."""
     x = np.asarray(x, dtype=np.float64)
     pos = np.sort(np.unique(E4M3_TABLE[np.isfinite(E4M3_TABLE) & (E4M3_TABLE >= 0)]))
     codes_pos = np.array([int(np.where(E4M3_TABLE == v)[0][0]) for v in pos], dtype=np.int64)
@@ -84,7 +84,7 @@ def f64_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
     take_hi = (dhi < dlo) | ((dhi == dlo) & ((codes_pos[idx] & 1) == 0))
     code = np.where(take_hi, codes_pos[idx], codes_pos[idx - 1])
     code = np.where(a <= 0.0, 0, code)
-    sign = np.where(np.signbit(x) & (code != 0), 0x80, 0)
+    sign = np.where(np.signbit(x), 0x80, 0)
     return (code | sign).astype(np.uint8)
 
 

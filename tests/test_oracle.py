@@ -134,3 +134,20 @@ def test_append_oracle_quantises_like_torch_and_skips_slots():
     np.testing.assert_array_equal(cache[1, 1], want[1])
     np.testing.assert_array_equal(cache[3, 15], want[3])
     assert not cache[0, 2].any()   # slot 2 untouched by the skipped token
+
+
+def test_e4m3_rounding_corners():
+    """Round-to-nearest-even at exact midpoints, subnormals and signed zero
+    match torch's float8_e4m3fn cast; magnitudes beyond 448 saturate to 448
+    (the append kernel's satfinite conversion)."""
+    pos = np.unique(R.E4M3_TABLE[np.isfinite(R.E4M3_TABLE) & (R.E4M3_TABLE >= 0)])
+    mids = (pos[:-1] + pos[1:]) / 2                       # exact ties
+    sub = np.linspace(2.0 ** -10, 2.0 ** -6, 97)          # subnormal range and its edge
+    x = np.concatenate([mids, -mids, sub, -sub, [0.0, -0.0, 447.9, -447.9]])
+    bits = R.f64_to_e4m3_bits(x)
+    tb = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(bits, tb)
+    # every tie went to the even code (last mantissa bit 0)
+    assert not (R.f64_to_e4m3_bits(mids) & 1).any()
+    sat = R.f64_to_e4m3_bits(np.array([448.0, 449.0, 1e4, -1e4]))
+    np.testing.assert_array_equal(R.e4m3_bits_to_f64(sat), [448.0, 448.0, 448.0, -448.0])
