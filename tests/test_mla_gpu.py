@@ -90,6 +90,20 @@ def test_mla_cfg4_full(cuda):
     assert_parity(out, lse, ro, rl, rows=rows)
 
 
+def test_mla_batch_larger_than_one_launch(cuda):
+    """More sequences than one launch's row table (384): the host slices the
+    batch, offsetting q, lengths, block table, out and lse per slice."""
+    rng = np.random.default_rng(11)
+    lens = rng.integers(1, 140, size=400).tolist()
+    lens[5] = 0
+    lens[390] = 0
+    x = _inputs(cuda, SMALL.scaled(batch=400), lens=lens)
+    out, lse = _run(x)
+    rows = [0, 5, 17, 383, 384, 385, 390, 399]
+    ro, rl = _oracle(x, rows=rows)
+    assert_parity(out[rows], lse[rows], ro, rl)
+
+
 def test_mla_rejects_unsupported_shapes(cuda):
     x = _inputs(cuda, SMALL, lens=[10])
     with pytest.raises(b200decode.B2DError):
