@@ -1,4 +1,4 @@
-"""Drop-in for the reference's own decode entry points (SURVEY row a9):
+"""Drop-in for the reference's own decode entry points:
 `cluster_decode_forward` / `cluster_decode_split_forward` over dense,
 contiguous q [B, H, 1, 128], k/v [B, H, S, 128]
 (cute_attention/cluster_decode/cluster_decode.py:114-147,

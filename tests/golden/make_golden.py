@@ -96,7 +96,9 @@ def sdpa_paged_fixture() -> None:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/Roofline-Analysis")
+    root = Path(sys.argv[1])
     split_merge_fixture(root)
     sdpa_paged_fixture()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
