@@ -422,8 +422,8 @@ def main():
             "scaling": "weak" if (args.scaling == "weak" or world == 1) else "strong",
             "vs_baseline": None,
             "pct_hbm_roofline": round(100 * tbs / (peak * world / 1e3), 2),
-            "dtype": "fp8-e4m3 KV, bf16 q, fp32 accumulate" if w0.kv_dtype == "fp8"
-                     else f"{w0.kv_dtype} in, fp32 accumulate",
+            "dtype": "fp8_e4m3" if w0.kv_dtype == "fp8" else w0.kv_dtype,
+            "accumulate": "fp32",
             "data": ("synthetic: seeded N(0,1) q/K/V, lengths ~ U[%d,%d], random page permutation"
                      % (w0.seqlen_lo, w0.seqlen_hi)),
             "config": {"workload": w0.name, "batch": w0.batch, "num_q_heads": w0.num_q_heads,
@@ -642,7 +642,8 @@ def run_mla(args, world, rank, local, w0):
             "us_per_step": round(ms * 1e3, 2), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
             "pct_hbm_roofline": round(100 * tbs / (hbm_peak * world / 1e3), 2),
-            "dtype": "bf16 in, fp32 accumulate (tcgen05)",
+            "dtype": "bf16",
+            "accumulate": "fp32 (tcgen05, TMEM)",
             "data": "synthetic: seeded N(0, 0.5) q and latent cache, lengths ~ U[%d,%d], random page permutation" % (w0.seqlen_lo, w0.seqlen_hi),
             "config": {"workload": w0.name, "batch": w0.batch, "num_heads": w0.num_heads,
                        "head_dim_qk": w0.head_dim_qk, "head_dim_v": w0.head_dim_v,
@@ -718,7 +719,9 @@ def run_reference_arm(args, world, rank, w0):
     line = {"impl": "reference", "metric": METRIC, "value": float(f"{tbs:.4g}"), "unit": "TB/s",
             "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
             "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16" if mla else w0.kv_dtype, "data": "synthetic",
+            "vs_baseline": None,
+            "dtype": "bf16" if mla else ("fp8_e4m3" if w0.kv_dtype == "fp8" else w0.kv_dtype),
+            "data": "synthetic",
             "config": {"workload": w0.name, "batch": w0.batch, "parallelism": "host cores",
                        "sample_sequences": n},
             "cpu_baseline": {"value": float(f"{tbs:.4g}"), "unit": "TB/s",
