@@ -172,3 +172,41 @@ def test_append_validation_on_host():
     assert lib.b2d_append_kv(C.byref(a), None) == -2                  # vLLM layout: 16-bit only
     a.kv_layout, a.num_tokens = _lib.B2D_KV_STRIDED, 0
     assert lib.b2d_append_kv(C.byref(a), None) == 0                   # nothing to append
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """include/b2d_decode.h compiles as C99 (what cgo / JNI / other FFI hosts
+    include) and a C program links against libb2d.so and calls host-only
+    entry points."""
+    import shutil
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    src = tmp_path / "probe.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "b2d_decode.h"
+int main(void) {
+  b2d_gqa_args a;
+  size_t n = 0;
+  int32_t ctas = 0, t = 0, hk = 0;
+  memset(&a, 0, sizeof a);
+  a.batch = 64; a.num_q_heads = 32; a.num_kv_heads = 8; a.head_dim = 128;
+  a.page_size = 16; a.max_pages_per_seq = 512; a.q_dtype = B2D_BF16; a.kv_dtype = B2D_BF16;
+  a.num_ctas = 296; a.kv_layout = B2D_KV_STRIDED;
+  if (b2d_gqa_workspace_bytes(&a, &n) != B2D_OK || n == 0) return 1;
+  if (b2d_gqa_plan(&a, &ctas, &t, &hk) != B2D_OK || ctas != 296) return 2;
+  if (b2d_decode_gqa(&a, NULL) != B2D_ERR_INVALID_ARG) return 3;   /* null pointers */
+  printf("%s %s\n", b2d_version(), b2d_error_string(B2D_ERR_UNSUPPORTED));
+  return 0;
+}
+''')
+    lib = _lib.LIB_PATH
+    exe = tmp_path / "probe"
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", f"-I{REPO / 'include'}", str(src),
+                        f"-L{lib.parent}", "-lb2d", f"-Wl,-rpath,{lib.parent}", "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, (r.returncode, r.stderr)
+    assert "sm_100a" in r.stdout
