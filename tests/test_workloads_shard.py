@@ -83,17 +83,18 @@ def _gather_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_tp_head_gather_layout_gloo_world2():
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_head_gather_layout_gloo(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_gather_worker, args=(r, world, port, q)) for r in range(world)]
     for p in ps:
         p.start()
     for p in ps:
         p.join(60)
-    res = dict(q.get(timeout=10) for _ in range(2))
-    assert res == {0: True, 1: True}
+    res = dict(q.get(timeout=10) for _ in range(world))
+    assert res == {r: True for r in range(world)}
 
 
 def test_decodebench_shape_matches_reference_record():
