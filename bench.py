@@ -4,27 +4,30 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2]
                     [--shard dp|tp] [--scaling weak|strong] [--impl b2d|reference]
 
-A step is one decode of the workload's whole batch (BASELINE config 2 by
-default: GQA paged, B=64, Hq=32, Hkv=8, D=128, bf16, lengths ~ U[1024, 8192],
-page 16, permuted pages).  For N > 1 the script runs under
+A step is one decode of the workload's whole batch.  The default workload
+is BASELINE config 5, the one the metric is quoted on at 1/2/4/8 GPUs: FP8
+KV GQA, B=256, Hq=32, Hkv=8, D=128, e4m3 K/V with per-KV-head fp32 scales,
+lengths ~ U[2048, 8192], page 16, permuted pages.  Other workloads by flag
+(--workload cfg1|cfg2|cfg3|cfg4).  For N > 1 the script runs under
 torch.distributed.run, one process per GPU over NCCL:
 
-* --scaling weak (default): every rank decodes its own full batch (seed +
-  rank); no collective inside the step.
-* --scaling strong --shard dp: the batch is split across ranks by a greedy
-  length balance; no collective inside the step.
+* --scaling strong --shard dp (default): the one batch is split across
+  ranks by a greedy length balance; no collective inside the step.
 * --scaling strong --shard tp: KV heads are split across ranks and the
   outputs are all-gathered over NCCL inside the step.
+* --scaling weak: every rank decodes its own full batch (seed + rank).
 
 Timing: W warm-up steps, then K steps between CUDA events on the launching
 stream, bracketed by barrier + synchronize, max over ranks.  The KV cache of
-one step (1.2 GB for config 2) is ~10x the 126 MB L2, so no flush is needed
-between steps.  `value` is achieved HBM TB/s over all ranks (algorithmic
+one step (2.7 GB for config 5, 1.2 GB for config 2) is 10-20x the 126 MB
+L2, so no flush is needed between steps at N=1; at N=8 each rank's share
+(~335 MB) is still ~2.7x L2.  `value` is achieved HBM TB/s over all ranks (algorithmic
 bytes / step time); `roofline` times the split-KV kernel alone.
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -53,9 +56,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b2d", "reference"], default="b2d")
-    ap.add_argument("--workload", default="cfg2")
+    ap.add_argument("--workload", default="cfg5")
     ap.add_argument("--shard", choices=["dp", "tp"], default="dp")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU work budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -148,6 +151,16 @@ def dist_setup():
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
+def gather_rows(vals, world: int, device):
+    """All ranks' lists of floats, in rank order (host-side, after timing)."""
+    if world == 1:
+        return [list(vals)]
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
 def reduce_over_ranks(x: float, world: int, device, op) -> float:
     if world == 1:
         return x
@@ -232,7 +245,7 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     SUM, MAX = dist.ReduceOp.SUM, dist.ReduceOp.MAX
 
     # ---- inputs ----
@@ -245,7 +258,7 @@ def main():
         xg = W.make_gqa_inputs(w0, dev)
         if args.shard == "dp":
             rows = shard.balance_sequences(xg["cache_seqlens"].tolist(), world)[rank]
-            x = shard.slice_gqa_inputs_by_batch(xg, rows)
+            x = shard.slice_gqa_inputs_by_batch(xg, rows, seed=rank)
             w = w0.scaled(batch=len(rows))
         else:
             x = shard.slice_gqa_inputs_by_heads(xg, world, rank)
@@ -264,19 +277,23 @@ def main():
                                      x["block_table"], x["softmax_scale"], k_scale=x["k_scale"],
                                      v_scale=x["v_scale"], flags=flags, **kw)
 
-    decoder = make_decoder()
+    hgather = (shard.HeadGather(w.batch, w.num_q_heads, w.head_dim, x["q"].dtype, dev)
+               if tp else None)
+    decoder = (make_decoder(out=hgather.out_local, lse=hgather.lse_local) if tp
+               else make_decoder())
 
     def step():
         out, lse = decoder.run()
-        if tp:
-            out, lse = shard.gather_heads(out, lse)
+        if tp:   # one packed all-gather into preallocated buffers
+            out, lse = hgather.gather()
         return out, lse
 
-    # launches of our kernels per step: split-KV + combine per batch slice
+    # launches of our kernels per step, as the library counts them (the
+    # split-KV kernel per batch slice, plus a combine kernel when the merge
+    # is not done in-kernel)
     n_ctas, chunk, hk_cta = b200decode.gqa_plan(x["q"], x["k_cache"], x["v_cache"],
                                                 x["cache_seqlens"], x["block_table"])
-    slices = max(1, math.ceil(w.batch * (w.num_kv_heads // hk_cta) / 2048))
-    launches_per_step = 2 * slices
+    launches_per_step = decoder.launches_per_run()
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -297,7 +314,8 @@ def main():
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ms = reduce_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, dev, MAX)
+    local_ms = ev0.elapsed_time(ev1) / args.steps
+    ms = reduce_over_ranks(local_ms, world, dev, MAX)
     total_bytes = reduce_over_ranks(local_bytes, world, dev, SUM)
     total_flops = reduce_over_ranks(W.gqa_flops(w, sl), world, dev, SUM)
     total_kv_ref = reduce_over_ranks(W.gqa_kv_bytes_reference(w, sl), world, dev, SUM)
@@ -319,6 +337,8 @@ def main():
 
     kk = max(5, args.steps)
     graph_ms = None
+    sampler_k = ClockSampler(local)
+    sampler_k.__enter__()
     if not tp:
         gdec = make_decoder().capture()
         for _ in range(3):
@@ -331,7 +351,8 @@ def main():
         torch.cuda.synchronize()
         graph_ms = ev0.elapsed_time(ev1) / kk
     kern_ms = timed(_lib.B2D_FLAG_SKIP_COMBINE, kk)
-    combine_ms = timed(_lib.B2D_FLAG_COMBINE_ONLY, kk)
+    combine_ms = timed(_lib.B2D_FLAG_COMBINE_ONLY, kk) if launches_per_step > 1 else 0.0
+    sampler_k.__exit__()
     peak, peak_kind = measured_hbm_peak()
     achieved_gbs = local_bytes / (kern_ms * 1e-3) / 1e9
 
@@ -349,12 +370,16 @@ def main():
         for _ in range(2):
             qd, sld, btd = (torch.empty_like(x["q"]), torch.empty_like(x["cache_seqlens"]),
                             torch.empty_like(x["block_table"]))
+            hg_j = (shard.HeadGather(w.batch, w.num_q_heads, w.head_dim, x["q"].dtype, dev)
+                    if tp else None)
             dec_j = b200decode.GqaDecoder(qd, x["k_cache"], x["v_cache"], sld, btd,
                                           x["softmax_scale"], k_scale=x["k_scale"],
-                                          v_scale=x["v_scale"])
+                                          v_scale=x["v_scale"],
+                                          out=hg_j.out_local if tp else None,
+                                          lse=hg_j.lse_local if tp else None)
             out_h = torch.empty((w.batch, hq_out, w.head_dim), dtype=x["q"].dtype).pin_memory()
             lse_h = torch.empty((w.batch, hq_out), dtype=torch.float32).pin_memory()
-            sets.append(dict(q=qd, sl=sld, bt=btd, dec=dec_j, out_h=out_h, lse_h=lse_h,
+            sets.append(dict(q=qd, sl=sld, bt=btd, dec=dec_j, hg=hg_j, out_h=out_h, lse_h=lse_h,
                              ready=torch.cuda.Event(), done=torch.cuda.Event(),
                              free=torch.cuda.Event()))
         h2d_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -370,7 +395,7 @@ def main():
             stream.wait_event(st["ready"])
             out, lse = st["dec"].run()
             if tp:
-                out, lse = shard.gather_heads(out, lse)
+                out, lse = st["hg"].gather()
             st["done"].record(stream)
             with torch.cuda.stream(d2h_stream):
                 d2h_stream.wait_event(st["done"])
@@ -401,6 +426,10 @@ def main():
                "d2h_bytes_per_step": int(reduce_over_ranks(d2h, world, dev, SUM)),
                "overlap": "double-buffered inputs/outputs; H2D and D2H on their own streams"}
 
+    # ---- per-rank numbers (the slowest rank sets the step time) ----
+    per_rank = gather_rows([local_ms * 1e3, float(sl.sum()), float(w.batch), kern_ms * 1e3,
+                            (graph_ms or 0.0) * 1e3], world, dev)
+
     # ---- CPU baseline (rank 0, N = 1) ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -411,7 +440,9 @@ def main():
                "sample": (f"torch.nn.functional.scaled_dot_product_attention on CPU (the call of "
                           f"decodebench/torch_sdpa_benchmark.py:100-102, enable_gqa) over the "
                           f"first {n} of {w.batch} sequences ({int(sl[:n].sum())} tokens), pages "
-                          f"gathered untimed; median of {reps} passes, {sec * 1e3:.1f} ms each"),
+                          f"gathered untimed; median of {reps} passes, {sec * 1e3:.1f} ms each; "
+                          f"TB/s = the sample's algorithmic bytes / its time"),
+               "extrapolated": n < w.batch,
                "cpu_model": cpu_model(), "os_cpu_count": os.cpu_count()}
 
     if rank == 0:
@@ -448,7 +479,14 @@ def main():
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
+            "launches_per_step": launches_per_step,
             "clocks": sampler.summary(),
+            "clocks_kernel_loops": sampler_k.summary(),
+            "per_rank": [{"rank": r, "us_per_step": round(v[0], 2), "tokens": int(v[1]),
+                          "sequences": int(v[2]), "kernel_us": round(v[3], 2),
+                          "cuda_graph_step_us": round(v[4], 2) if v[4] else None}
+                         for r, v in enumerate(per_rank)],
+            "slowest_rank": int(max(range(len(per_rank)), key=lambda r: per_rank[r][0])),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -496,7 +534,7 @@ def run_mla(args, world, rank, local, w0):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     SUM, MAX = dist.ReduceOp.SUM, dist.ReduceOp.MAX
     w = w0.scaled(seed=w0.seed + rank) if world > 1 else w0
     x = W.make_mla_inputs(w, dev)

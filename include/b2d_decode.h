@@ -60,10 +60,17 @@ enum b2d_status {
 /* Launch flags, for measuring the two kernels of a decode separately.
  * SKIP_COMBINE enqueues only the split-KV kernel (rows split across CTAs are
  * then left as partials in the workspace); COMBINE_ONLY enqueues only the
- * merge, over the partials the previous identical call left. */
+ * merge, over the partials the previous identical call left.  When the GQA
+ * plan merges inside the split-KV kernel (many rows per CTA wave), there is
+ * no combine kernel: SKIP_COMBINE changes nothing and COMBINE_ONLY enqueues
+ * nothing.  TEST_NO_LOADS is for testing the bounded waits: the producer
+ * issues no loads, so every consumer wait runs out after wait_limit_us,
+ * records B2D_ERR_DEVICE_TIMEOUT in the status word and returns (no copy is
+ * in flight when the kernel ends); out and lse are then undefined. */
 enum b2d_flags {
   B2D_FLAG_SKIP_COMBINE = 1,
-  B2D_FLAG_COMBINE_ONLY = 2
+  B2D_FLAG_COMBINE_ONLY = 2,
+  B2D_FLAG_TEST_NO_LOADS = 4
 };
 
 /* Paged-cache layouts (b2d_gqa_args.kv_layout). */
@@ -131,11 +138,17 @@ typedef struct b2d_gqa_args {
   int32_t num_ctas;        /* 0 = one resident wave on this device          */
   int32_t flags;           /* B2D_FLAG_* (0 = normal decode)                */
   int32_t kv_layout;       /* B2D_KV_* (0 = strided NHD/HND)                */
-  int32_t reserved;
+  int32_t wait_limit_us;   /* in-kernel wait limit, microseconds (0 = 2 s)  */
 } b2d_gqa_args;
 
 /* Workspace bytes that b2d_decode_gqa needs for these arguments (pointers
- * may be NULL here; only sizes, dtypes and num_ctas are read). */
+ * may be NULL here; only sizes, dtypes and num_ctas are read).  Every
+ * workspace starts with a 256-byte status word and 64 KiB of split-merge
+ * arrival counters (B2D_WORKSPACE_HEADER_BYTES in all); both must be zero
+ * before the first call (cudaMemset once after allocating).  The kernels
+ * leave them zero; b2d_check_device_status(clear = 1) re-zeroes them after a
+ * device error. */
+#define B2D_WORKSPACE_HEADER_BYTES 65792
 int b2d_gqa_workspace_bytes(const b2d_gqa_args* args, size_t* bytes);
 
 /* Enqueue the decode (split-KV kernel, then the LSE combine when a
@@ -186,7 +199,8 @@ typedef struct b2d_mla_args {
   size_t workspace_bytes;
   int32_t num_ctas;        /* 0 = auto                                      */
   int32_t flags;           /* B2D_FLAG_* (0 = normal decode)                */
-  int32_t reserved[2];
+  int32_t wait_limit_us;   /* in-kernel wait limit, microseconds (0 = 2 s)  */
+  int32_t reserved;
 } b2d_mla_args;
 
 int b2d_mla_workspace_bytes(const b2d_mla_args* args, size_t* bytes);
@@ -234,6 +248,13 @@ int b2d_append_kv(const b2d_append_args* args, void* stream);
  * Synchronises `stream`.  Returns 0 or the matching negative b2d_status.
  */
 int b2d_check_device_status(void* workspace, int clear, void* stream);
+/*
+ * The same read-back for b2d_decode_gqa_static_scratch, whose status word
+ * lives in the library's own scratch array on the current device (a caller
+ * never sees that array's address).  No counterpart in the reference.
+ * Returns B2D_OK when no call on this device has used the array yet.
+ */
+int b2d_static_scratch_check_status(int clear, void* stream);
 
 /* Split plan the GQA kernel would use: number of CTAs (0 when num_ctas is 0:
  * one resident wave, resolved at launch from the kernel's occupancy), KV
@@ -241,6 +262,12 @@ int b2d_check_device_status(void* workspace, int clear, void* stream);
 int b2d_gqa_plan(const b2d_gqa_args* args, int32_t* num_ctas,
                  int32_t* chunk_tokens, int32_t* kv_heads_per_cta);
 
+/* Number of kernel launches one b2d_decode_gqa call with these arguments
+ * enqueues (the split-KV kernel per batch slice, plus a combine kernel per
+ * slice when the merge is not done in-kernel).  Launches nothing; needs a
+ * current device (the plan depends on its SM count and occupancy).  No
+ * counterpart in the reference. */
+int b2d_gqa_launch_count(const b2d_gqa_args* args, int32_t* launches);
 const char* b2d_error_string(int status);
 const char* b2d_version(void);
 

@@ -106,14 +106,14 @@ def dense_decode(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float):
     lse = np.full((hq,), -np.inf, dtype=np.float64)
     if k.shape[1] == 0:
         return out, lse
-    for h in range(hq):
-        g = h // group
-        s = (k[g] @ q[h]) * scale
-        m = s.max()
+    for g in range(hkv):   # the `group` query heads of KV head g at once
+        hs = slice(g * group, (g + 1) * group)
+        s = (q[hs] @ k[g].T) * scale            # [group, S]
+        m = s.max(axis=1, keepdims=True)
         e = np.exp(s - m)
-        den = e.sum()
-        out[h] = (e @ v[g]) / den
-        lse[h] = m + np.log(den)
+        den = e.sum(axis=1)
+        out[hs] = (e @ v[g]) / den[:, None]
+        lse[hs] = m[:, 0] + np.log(den)
     return out, lse
 
 

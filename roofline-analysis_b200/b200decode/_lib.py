@@ -12,7 +12,8 @@ LIB_PATH = Path(__file__).resolve().parent / "_native" / "libb2d.so"
 
 B2D_KV_STRIDED, B2D_KV_VLLM = 0, 1
 B2D_BF16, B2D_FP16, B2D_FP8_E4M3, B2D_FP32 = 0, 1, 2, 3
-B2D_FLAG_SKIP_COMBINE, B2D_FLAG_COMBINE_ONLY = 1, 2
+B2D_FLAG_SKIP_COMBINE, B2D_FLAG_COMBINE_ONLY, B2D_FLAG_TEST_NO_LOADS = 1, 2, 4
+B2D_WORKSPACE_HEADER_BYTES = 65792
 
 EXPORTED = (
     "b2d_gqa_workspace_bytes",
@@ -46,7 +47,7 @@ class GqaArgs(C.Structure):
         ("softmax_scale", C.c_float),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
         ("num_ctas", C.c_int32), ("flags", C.c_int32), ("kv_layout", C.c_int32),
-        ("reserved", C.c_int32),
+        ("wait_limit_us", C.c_int32),
     ]
 
 
@@ -63,7 +64,8 @@ class MlaArgs(C.Structure):
         ("head_dim_v", C.c_int32), ("page_size", C.c_int32), ("max_pages_per_seq", C.c_int32),
         ("dtype", C.c_int32), ("softmax_scale", C.c_float),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
-        ("num_ctas", C.c_int32), ("flags", C.c_int32), ("reserved", C.c_int32 * 2),
+        ("num_ctas", C.c_int32), ("flags", C.c_int32), ("wait_limit_us", C.c_int32),
+        ("reserved", C.c_int32),
     ]
 
 
@@ -103,6 +105,8 @@ def load() -> C.CDLL:
     lib.b2d_decode_mla.argtypes = [C.POINTER(MlaArgs), C.c_void_p]
     lib.b2d_append_kv.argtypes = [C.POINTER(AppendArgs), C.c_void_p]
     lib.b2d_check_device_status.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    lib.b2d_static_scratch_check_status.argtypes = [C.c_int, C.c_void_p]
+    lib.b2d_gqa_launch_count.argtypes = [C.POINTER(GqaArgs), C.POINTER(C.c_int32)]
     lib.b2d_gqa_plan.argtypes = [C.POINTER(GqaArgs), C.POINTER(C.c_int32), C.POINTER(C.c_int32),
                                  C.POINTER(C.c_int32)]
     lib.b2d_error_string.restype = C.c_char_p

@@ -35,16 +35,31 @@ def library_path() -> str:
 
 
 class DecodeWorkspace:
-    """Caller-owned device scratch for split partials (plus the 256-byte
-    status word at its head).  Grows on demand; one per device by default."""
+    """Caller-owned device scratch for split partials.  Its head is the
+    library's workspace header (status word and split-merge arrival
+    counters), which must be zero before first use: buffers are allocated
+    with torch.zeros.  Grows on demand.
 
-    def __init__(self, device: torch.device, nbytes: int = 0):
+    The default workspaces are one per (device, stream): two decodes
+    enqueued on different streams never share partials.  A workspace is
+    allocated, and re-allocated when it grows, on the stream it serves, so
+    torch's caching allocator recycles the old buffer only in that stream's
+    order (after the last decode that read it)."""
+
+    def __init__(self, device: torch.device, nbytes: int = 0, stream=None):
         self.device = torch.device(device)
-        self.buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=self.device)
+        self.stream = stream
+        self.buf = self._alloc(max(nbytes, 1 << 20))
+
+    def _alloc(self, n: int) -> torch.Tensor:
+        if self.stream is None:
+            return torch.zeros(n, dtype=torch.uint8, device=self.device)
+        with torch.cuda.stream(self.stream):
+            return torch.zeros(n, dtype=torch.uint8, device=self.device)
 
     def ensure(self, nbytes: int) -> "DecodeWorkspace":
         if self.buf.numel() < nbytes:
-            self.buf = torch.zeros(int(nbytes * 1.25) + 4096, dtype=torch.uint8, device=self.device)
+            self.buf = self._alloc(int(nbytes * 1.25) + 4096)
         return self
 
     @property
@@ -60,11 +75,17 @@ _ws_lock = threading.Lock()
 _ws: dict = {}
 
 
-def _default_ws(device: torch.device) -> DecodeWorkspace:
-    key = (device.type, device.index)
+def _default_ws(device: torch.device, stream=None) -> DecodeWorkspace:
+    """The default workspace of (device, stream); stream defaults to the
+    device's current torch stream."""
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
     with _ws_lock:
         if key not in _ws:
-            _ws[key] = DecodeWorkspace(device)
+            _ws[key] = DecodeWorkspace(device, stream=stream)
         return _ws[key]
 
 
@@ -165,7 +186,7 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
            v_scale: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
            lse: Optional[torch.Tensor] = None, kv_layout: str = "NHD",
            num_ctas: Optional[int] = None, workspace: Optional[DecodeWorkspace] = None,
-           flags: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+           flags: int = 0, wait_limit_us: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
     """Paged GQA/MHA/MQA decode for one query token per sequence.
 
     q: [B, Hq, D] or [B, 1, Hq, D] (bf16/fp16).  k_cache, v_cache:
@@ -176,7 +197,8 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     cache_seqlens: int32 [B]; block_table: int32 [B, max_pages].
     softmax_scale defaults to 1/sqrt(D).  Returns out (shape of q, q's dtype)
     and lse [B, Hq] fp32 (natural log).  `flags` (B2D_FLAG_*) exists for
-    timing the split-KV and combine kernels separately.
+    timing the split-KV and combine kernels separately and for testing;
+    `wait_limit_us` bounds every in-kernel wait (0 = the 2 s default).
     """
     if not q.is_cuda:
         raise RuntimeError("b200decode.decode needs CUDA tensors (there is no CPU path)")
@@ -192,6 +214,7 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     a = _gqa_args(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, k_scale,
                   v_scale, out3, lse, kv_layout, num_ctas)
     a.flags = int(flags)
+    a.wait_limit_us = int(wait_limit_us)
     ws = workspace or _default_ws(q.device)
     need = C.c_size_t(0)
     _check(lib.b2d_gqa_workspace_bytes(C.byref(a), C.byref(need)), "b2d_gqa_workspace_bytes")
@@ -210,7 +233,9 @@ class GqaDecoder:
     block_table / the caches in place between runs (shapes fixed).
 
     run() enqueues one decode on the current stream and returns (out, lse).
-    capture() records run() into a CUDA graph; replay() launches it.
+    capture() records run() into a CUDA graph; replay() launches it.  The
+    decoder's workspace is bound at construction (the default one of the
+    stream current then): run it on that stream, or pass `workspace`.
     """
 
     def __init__(self, q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale=None, *,
@@ -247,6 +272,13 @@ class GqaDecoder:
         if rc:
             raise B2DError(rc, "b2d_decode_gqa")
         return self.out, self.lse
+
+    def launches_per_run(self) -> int:
+        """Kernel launches one run() enqueues (split-KV kernel, plus the
+        combine kernel when the merge is not done in-kernel)."""
+        n = C.c_int32(0)
+        _check(self._lib.b2d_gqa_launch_count(self._argp, C.byref(n)), "b2d_gqa_launch_count")
+        return n.value
 
     def capture(self):
         """Record one run() into a CUDA graph (after a warm-up run, which does
@@ -389,12 +421,20 @@ def append_kv(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_c
 def check_device_status(workspace: Optional[DecodeWorkspace] = None, device=None,
                         clear: bool = True) -> None:
     """Synchronise and raise B2DError if a kernel recorded a timeout or an
-    out-of-range page id in the workspace status word."""
+    out-of-range page id in a workspace status word.  Without `workspace`,
+    every default workspace of the device (one per stream used) is read."""
     lib = _lib.load()
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     if device.type == "cuda" and device.index is None:
         device = torch.device("cuda", torch.cuda.current_device())
-    ws = workspace or _default_ws(device)
+    if workspace is not None:
+        spaces = [workspace]
+    else:
+        _default_ws(device)   # at least the current stream's
+        with _ws_lock:
+            spaces = [w for (idx, _), w in _ws.items() if idx == device.index]
     stream = torch.cuda.current_stream(device).cuda_stream
-    _check(lib.b2d_check_device_status(C.c_void_p(ws.ptr), int(clear), C.c_void_p(stream)),
-           "device status")
+    torch.cuda.synchronize(device)
+    for ws in spaces:
+        _check(lib.b2d_check_device_status(C.c_void_p(ws.ptr), int(clear), C.c_void_p(stream)),
+               "device status")

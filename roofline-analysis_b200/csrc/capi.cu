@@ -1,6 +1,7 @@
 // capi.cu — library-wide C entry points: error strings, version, and the
 // device status word read-back.
 #include "b2d_decode.h"
+#include "common.cuh"
 #include "host_common.h"
 
 extern "C" const char* b2d_error_string(int status) {
@@ -28,10 +29,16 @@ extern "C" int b2d_check_device_status(void* workspace, int clear, void* stream)
     return B2D_ERR_CUDA;
   if (cudaStreamSynchronize(st) != cudaSuccess) return B2D_ERR_CUDA;
   if (clear && word != 0) {
-    if (cudaMemsetAsync(workspace, 0, sizeof(int), st) != cudaSuccess) return B2D_ERR_CUDA;
+    // A kernel that gave up waiting may have left split-merge arrival
+    // counters half counted: clear them with the word.
+    const size_t n = (word & 1) ? b2d::kWsHeaderBytes : sizeof(int);
+    if (cudaMemsetAsync(workspace, 0, n, st) != cudaSuccess) return B2D_ERR_CUDA;
     if (cudaStreamSynchronize(st) != cudaSuccess) return B2D_ERR_CUDA;
   }
   if (word & 1) return B2D_ERR_DEVICE_TIMEOUT;
   if (word & 2) return B2D_ERR_DEVICE_BOUNDS;
   return B2D_OK;
 }
+
+static_assert(b2d::kWsHeaderBytes == B2D_WORKSPACE_HEADER_BYTES,
+              "workspace header size in b2d_decode.h");

@@ -15,11 +15,19 @@ namespace b2d {
 constexpr int kStatusTimeout = 1;
 constexpr int kStatusBounds = 2;
 
-// A wait on an mbarrier gives up after this many nanoseconds of wall time
-// (globaltimer).  No legitimate wait in these kernels comes near it: every
-// wait is for a TMA copy already issued or for a stage the consumers release
-// after a few microseconds of arithmetic.
+// By default a wait on an mbarrier gives up after this many nanoseconds of
+// wall time (globaltimer).  No legitimate wait in these kernels comes near
+// it: every wait is for a TMA copy already issued or for a stage the
+// consumers release after a few microseconds of arithmetic.  Callers may
+// pass a shorter limit per launch (b2d_gqa_args.wait_limit_us).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+// Workspace header shared by every decode entry point: the status word
+// (256 bytes), then the arrival counters of the in-kernel split merge
+// (kMergeCounters int32, zero between calls).  Everything else follows.
+constexpr size_t kStatusBytes = 256;
+constexpr int kMergeCounters = 16384;
+constexpr size_t kWsHeaderBytes = kStatusBytes + (size_t)kMergeCounters * 4;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,11 +72,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: true when the phase with `parity` completed, false when the
 // wall-time limit ran out (the caller then records kStatusTimeout and exits).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
   return true;
 }

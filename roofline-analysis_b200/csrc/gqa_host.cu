@@ -15,7 +15,6 @@ namespace b2d {
 constexpr int kMaxRowsPerLaunch = 2048;
 // Default shared-memory budget for the K/V stage ring of one CTA.
 constexpr size_t kStageRingBytes = 96 * 1024;
-constexpr size_t kStatusBytes = 256;
 // Most resident CTAs per SM the workspace is sized for.
 constexpr int kMaxCtasPerSm = 4;
 
@@ -34,6 +33,7 @@ struct GqaPlan {
   uint32_t stage_bytes;
   size_t smem;
   size_t off_row_start, off_part_lse, off_part_o, ws_bytes;
+  int* launch_count;  // when set: count the launches a call makes, launch nothing
 };
 
 static int kv_elem_bytes(int kv_dtype) { return kv_dtype == B2D_FP8_E4M3 ? 1 : 2; }
@@ -57,6 +57,9 @@ static int validate(const b2d_gqa_args* a, bool need_pointers) {
   const int group = a->num_q_heads / a->num_kv_heads;
   if (group > 32) return B2D_ERR_UNSUPPORTED;
   if (a->page_size > (1 << 24)) return B2D_ERR_TOO_LARGE;
+  // Token positions (max_pages_per_seq * page_size) are 32-bit in the kernels.
+  if ((int64_t)a->max_pages_per_seq * a->page_size > (int64_t)INT32_MAX) return B2D_ERR_TOO_LARGE;
+  if (a->wait_limit_us < 0) return B2D_ERR_INVALID_ARG;
   if (a->kv_layout != B2D_KV_STRIDED && a->kv_layout != B2D_KV_VLLM) return B2D_ERR_INVALID_ARG;
   if (a->kv_layout == B2D_KV_VLLM) {
     // K [blocks, Hkv, D/8, P, 8] and V [blocks, Hkv, D, P]: the kernel reads
@@ -180,7 +183,7 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
   pl->ctas = ctas;
   const int hqc = pl->hk * group;
   const size_t segs = (size_t)pl->rows_per_launch + ctas_cap;
-  pl->off_row_start = kStatusBytes;
+  pl->off_row_start = kWsHeaderBytes;
   pl->off_part_lse = align_up(pl->off_row_start + (size_t)(pl->rows_per_launch + 1) * 4, 256);
   pl->off_part_o = align_up(pl->off_part_lse + segs * hqc * 4, 256);
   pl->ws_bytes = align_up(pl->off_part_o + segs * hqc * (size_t)a->head_dim * 4, 256);
@@ -202,11 +205,26 @@ static int launch_k(Kern kern, void (*combine)(const GqaParams, int, int), const
     per_sm = per_sm < 1 ? 1 : (per_sm > kMaxCtasPerSm ? kMaxCtasPerSm : per_sm);
     ctas = sms * per_sm;
   }
+  const int R = p.B * p.HG;
+  // The split merge runs inside the split-KV kernel (the last warp to finish
+  // a split row merges it) when rows are split over few CTAs each; with few
+  // rows (small batches, rows over ~100 CTAs) the multi-warp combine kernel
+  // spreads the merges instead.  B2D_GQA_FUSED_MERGE=0/1 forces either.
+  static const int fused_env = env_int("B2D_GQA_FUSED_MERGE", -1);
+  const bool fused = pl.mma && (fused_env >= 0 ? fused_env != 0 : (int64_t)R * 7 >= ctas) &&
+                     (int64_t)R * p.NW <= kMergeCounters;
+  if (pl.launch_count != nullptr) {
+    *pl.launch_count += (flags & B2D_FLAG_COMBINE_ONLY) ? 0 : 1;
+    if (!fused && !(flags & B2D_FLAG_SKIP_COMBINE) && R * pl.hk * pl.group > 0) ++*pl.launch_count;
+    return B2D_OK;
+  }
   if (!(flags & B2D_FLAG_COMBINE_ONLY)) {
-    kern<<<ctas, threads, pl.smem, st>>>(tk, tv, p);
+    GqaParams pk = p;
+    pk.merge_count = fused ? p.merge_count : nullptr;
+    kern<<<ctas, threads, pl.smem, st>>>(tk, tv, pk);
     if (cudaGetLastError() != cudaSuccess) return B2D_ERR_CUDA;
   }
-  const int R = p.B * p.HG;
+  if (fused) return B2D_OK;
   const int64_t merges = (int64_t)R * pl.hk * pl.group;
   const int wpp = combine_warps_per_merge(merges);
   const int blocks = (int)((merges + 8 / wpp - 1) / (8 / wpp));
@@ -338,7 +356,7 @@ extern "C" int b2d_gqa_workspace_bytes(const b2d_gqa_args* a, size_t* bytes) {
   int rc = validate(a, false);
   if (rc) return rc;
   if (!bytes) return B2D_ERR_INVALID_ARG;
-  GqaPlan pl;
+  GqaPlan pl{};
   rc = make_plan(a, &pl);
   if (rc) return rc;
   *bytes = pl.ws_bytes;
@@ -349,7 +367,7 @@ extern "C" int b2d_gqa_plan(const b2d_gqa_args* a, int32_t* num_ctas, int32_t* c
                             int32_t* kv_heads_per_cta) {
   int rc = validate(a, false);
   if (rc) return rc;
-  GqaPlan pl;
+  GqaPlan pl{};
   rc = make_plan(a, &pl);
   if (rc) return rc;
   if (num_ctas) *num_ctas = pl.ctas;
@@ -358,20 +376,23 @@ extern "C" int b2d_gqa_plan(const b2d_gqa_args* a, int32_t* num_ctas, int32_t* c
   return B2D_OK;
 }
 
-extern "C" int b2d_decode_gqa(const b2d_gqa_args* a, void* stream) {
-  int rc = validate(a, true);
+static int decode_gqa(const b2d_gqa_args* a, void* stream, int* launch_count) {
+  int rc = validate(a, launch_count == nullptr);
   if (rc) return rc;
   if (a->batch == 0) return B2D_OK;
-  GqaPlan pl;
+  GqaPlan pl{};
   rc = make_plan(a, &pl);
   if (rc) return rc;
-  if (!a->workspace || a->workspace_bytes < pl.ws_bytes) return B2D_ERR_WORKSPACE;
-  if ((uintptr_t)a->workspace & 255) return B2D_ERR_ALIGNMENT;
-  CUtensorMap tk, tv;
-  if (encode_kv_map(&tk, a->k_cache, a, a->k_stride_page, a->k_stride_tok, a->k_stride_head, pl,
+  pl.launch_count = launch_count;
+  if (launch_count == nullptr) {
+    if (!a->workspace || a->workspace_bytes < pl.ws_bytes) return B2D_ERR_WORKSPACE;
+    if ((uintptr_t)a->workspace & 255) return B2D_ERR_ALIGNMENT;
+  }
+  CUtensorMap tk{}, tv{};
+  if (launch_count == nullptr && (encode_kv_map(&tk, a->k_cache, a, a->k_stride_page, a->k_stride_tok, a->k_stride_head, pl,
                     false) ||
       encode_kv_map(&tv, a->v_cache, a, a->v_stride_page, a->v_stride_tok, a->v_stride_head, pl,
-                    true))
+                    true)))
     return B2D_ERR_CUDA;
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -394,6 +415,9 @@ extern "C" int b2d_decode_gqa(const b2d_gqa_args* a, void* stream) {
     p.k_scale = a->k_scale;
     p.v_scale = a->v_scale;
     p.status = reinterpret_cast<int*>(ws);
+    p.merge_count = reinterpret_cast<int32_t*>(ws + kStatusBytes);
+    p.wait_ns = a->wait_limit_us > 0 ? (unsigned long long)a->wait_limit_us * 1000ull : kWaitLimitNs;
+    p.no_loads = (a->flags & B2D_FLAG_TEST_NO_LOADS) ? 1 : 0;
     p.row_start_g = reinterpret_cast<int32_t*>(ws + pl.off_row_start);
     p.part_lse = reinterpret_cast<float*>(ws + pl.off_part_lse);
     p.part_o = reinterpret_cast<float*>(ws + pl.off_part_o);
@@ -420,5 +444,18 @@ extern "C" int b2d_decode_gqa(const b2d_gqa_args* a, void* stream) {
     }
     if (rc) return rc;
   }
+  return B2D_OK;
+}
+
+extern "C" int b2d_decode_gqa(const b2d_gqa_args* a, void* stream) {
+  return decode_gqa(a, stream, nullptr);
+}
+
+extern "C" int b2d_gqa_launch_count(const b2d_gqa_args* a, int32_t* launches) {
+  if (!launches) return B2D_ERR_INVALID_ARG;
+  int n = 0;
+  const int rc = decode_gqa(a, nullptr, &n);
+  if (rc) return rc;
+  *launches = n;
   return B2D_OK;
 }

@@ -60,7 +60,11 @@ struct GqaParams {
   float* part_o;     // [(R + G) * HQC * D]
   float* part_lse;   // [(R + G) * HQC], log2 units
   int32_t* row_start_g;  // [R + 1], written by CTA 0 for the combine
+  int32_t* merge_count;  // [R * NW] arrival counters of the in-kernel merge, or
+                         // null when a separate combine kernel merges
   int* status;
+  unsigned long long wait_ns;  // bounded-wait limit of every mbarrier wait
+  int no_loads;                // test only: the producer issues no loads
   int B, Hq, Hkv, group, HK, HG, P, T, stages, NW, WPH;
   int num_pages, max_pages;
   float scale_log2;        // softmax_scale * log2(e)
@@ -245,6 +249,7 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
 
   if (warp == p.NW) {
     // ---------------- producer warp ----------------
+    if (p.no_loads) return;  // test flag: every consumer wait then runs out
     const uint64_t policy = policy_evict_first();
     bool ok = true;
     int s = 0;
@@ -273,7 +278,7 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
         const int off = __shfl_sync(0xffffffffu, my_off, k);
         const int h0 = __shfl_sync(0xffffffffu, my_h0, k);
         if (lane == 0 && ok) {
-          if (!mbar_wait(empty + s, ph ^ 1u)) {
+          if (!mbar_wait(empty + s, ph ^ 1u, p.wait_ns)) {
             record_status(p.status, kStatusTimeout);
             ok = false;
           } else {
@@ -505,7 +510,7 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
       start_row(row);
       cur_row = row;
     }
-    if (!mbar_wait(full + s, ph)) {
+    if (!mbar_wait(full + s, ph, p.wait_ns)) {
       record_status(p.status, kStatusTimeout);
       return;
     }
@@ -529,6 +534,75 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
     }
   }
   if (cur_row >= 0) finish_row(cur_row);
+}
+
+// One warp merges the split partials of query heads [qh_row0, qh_row0 + nh)
+// of row (b, hg) over segments seg0 .. seg0 + nseg - 1 (the LSE rule of
+// cluster_decode_reduce.py:67-91 in log2 units) and writes out and lse.
+// Used by the split-KV kernel's last-arriving warp (the partials of other
+// CTAs are read past L1, after the acquire fence of the arrival counter).
+template <int D, typename QT>
+__device__ __forceinline__ void warp_merge_heads(const GqaParams& p, int b, int hg, int HQC,
+                                                 int qh_row0, int nh, int64_t seg0, int nseg) {
+  constexpr float kLn2 = 0.69314718055994530942f;
+  constexpr int EPL = D / 32;
+  constexpr int U = D >= 256 ? 4 : 8;
+  const int lane = threadIdx.x & 31;
+  for (int hw = 0; hw < nh; ++hw) {
+    const int qh_row = qh_row0 + hw;
+    float mx = -INFINITY;
+    for (int j = lane; j < nseg; j += 32) mx = fmaxf(mx, __ldcg(p.part_lse + (seg0 + j) * HQC + qh_row));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    float wsum = 0.f;
+    for (int j0 = 0; j0 < nseg; j0 += U) {
+      float lv[U];
+      float2 v[U][EPL / 2];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + u < nseg ? j0 + u : nseg - 1;
+        lv[u] = __ldcg(p.part_lse + (seg0 + j) * HQC + qh_row);
+        const float2* src = reinterpret_cast<const float2*>(p.part_o + ((seg0 + j) * HQC + qh_row) * D + lane * EPL);
+#pragma unroll
+        for (int e = 0; e < EPL / 2; ++e) v[u][e] = __ldcg(src + e);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float w = (j0 + u < nseg) ? fast_exp2(lv[u] - mx) : 0.f;
+        wsum += w;
+#pragma unroll
+        for (int e = 0; e < EPL / 2; ++e) {
+          acc[2 * e] += w * v[u][e].x;
+          acc[2 * e + 1] += w * v[u][e].y;
+        }
+      }
+    }
+    const int qh = hg * HQC + qh_row;
+    QT* dst = reinterpret_cast<QT*>(p.out) + (int64_t)b * p.o_sb + (int64_t)qh * p.o_sh + lane * EPL;
+    const float inv = 1.f / wsum;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = QT(acc[e] * inv);
+    if (p.lse != nullptr && lane == 0) p.lse[(int64_t)b * p.lse_sb + qh] = (mx + fast_log2(wsum)) * kLn2;
+  }
+}
+
+// One warp writes out = 0, lse = -inf for query heads [qh_row0, qh_row0 + nh)
+// of a zero-length row (b, hg).
+template <int D, typename QT>
+__device__ __forceinline__ void warp_zero_heads(const GqaParams& p, int b, int hg, int HQC,
+                                                int qh_row0, int nh) {
+  constexpr int EPL = D / 32;
+  const int lane = threadIdx.x & 31;
+  for (int hw = 0; hw < nh; ++hw) {
+    const int qh = hg * HQC + qh_row0 + hw;
+    QT* dst = reinterpret_cast<QT*>(p.out) + (int64_t)b * p.o_sb + (int64_t)qh * p.o_sh + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = QT(0.f);
+    if (p.lse != nullptr && lane == 0) p.lse[(int64_t)b * p.lse_sb + qh] = -INFINITY;
+  }
 }
 
 // Merge the split partials of every row that more than one CTA touched

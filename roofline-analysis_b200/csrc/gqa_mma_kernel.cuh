@@ -177,6 +177,17 @@ __global__ void __launch_bounds__(32 * 9, 1)
   }
   const int64_t W = row_start[R];
   const int G = W < (int64_t)gridDim.x ? (int)W : (int)gridDim.x;
+  if (p.merge_count != nullptr && warp < p.NW) {
+    // No combine kernel follows: rows of zero length get out = 0, lse = -inf
+    // here, spread over the CTAs; each consumer warp writes its own heads.
+    const int hk_w = warp / p.WPH, gw_w = p.group / p.WPH;
+    for (int r = cta; r < R; r += gridDim.x) {
+      if (row_start[r + 1] != row_start[r]) continue;
+      const int b = r / p.HG;
+      warp_zero_heads<D, QT>(p, b, r - b * p.HG, p.HK * p.group,
+                             hk_w * p.group + (warp - hk_w * p.WPH) * gw_w, gw_w);
+    }
+  }
   if (W == 0 || cta >= G) return;
   const int x0 = (int)((int64_t)cta * W / G);
   const int x1 = (int)((int64_t)(cta + 1) * W / G);
@@ -184,6 +195,8 @@ __global__ void __launch_bounds__(32 * 9, 1)
 
   if (warp == p.NW) {
     // ---------------- producer warp (one K and one V box per chunk) --------
+    // (test flag no_loads: issue nothing, so every consumer wait runs out)
+    if (p.no_loads) return;
     const uint64_t policy = policy_evict_first();
     bool ok = true;
     int s = 0;
@@ -211,7 +224,7 @@ __global__ void __launch_bounds__(32 * 9, 1)
         const int off = __shfl_sync(0xffffffffu, my_off, k);
         const int h0 = __shfl_sync(0xffffffffu, my_h0, k);
         if (lane == 0 && ok) {
-          if (!mbar_wait(empty + s, ph ^ 1u)) {
+          if (!mbar_wait(empty + s, ph ^ 1u, p.wait_ns)) {
             record_status(p.status, kStatusTimeout);
             ok = false;
           } else {
@@ -342,6 +355,23 @@ __global__ void __launch_bounds__(32 * 9, 1)
       }
     }
     (void)kvh;
+    if (cf != cl && p.merge_count != nullptr) {
+      // In-kernel merge: every warp that wrote a partial of these heads
+      // counts itself in (release: fence, then the atomic); the warp that
+      // arrives last (acquire: the atomic, then a fence) merges all
+      // cl - cf + 1 partials and re-arms the counter for the next call.
+      __threadfence();
+      __syncwarp();
+      int* cnt = p.merge_count + (int64_t)row * p.NW + warp;
+      int old = 0;
+      if (lane == 0) old = atomicAdd(cnt, 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == cl - cf) {
+        __threadfence();
+        warp_merge_heads<D, QT>(p, b, hg, HQC, qh_row0, GW, (int64_t)row + cf, cl - cf + 1);
+        if (lane == 0) *cnt = 0;
+      }
+    }
   };
 
   int row = find_row(row_start, R, x0);
@@ -355,7 +385,7 @@ __global__ void __launch_bounds__(32 * 9, 1)
       start_row(row);
       cur_row = row;
     }
-    if (!mbar_wait(full + s, ph)) {
+    if (!mbar_wait(full + s, ph, p.wait_ns)) {
       record_status(p.status, kStatusTimeout);
       return;
     }

@@ -16,8 +16,12 @@
 //     b2d_decode_gqa with a caller-provided workspace has no such limit).
 //     16 MiB covers BASELINE configs 2, 3 and 5 (at most ~9.1 MB).
 //   * The first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (with that device current) and clears the status
-//     word; make that first call before any stream capture.
+//     cudaGetSymbolAddress (with that device current) and clears the
+//     workspace header (status word and split-merge counters); make that
+//     first call before any stream capture.
+//   * In-kernel errors (a wait that ran out, a page id out of range) are
+//     recorded in the array's status word: read and clear them with
+//     b2d_static_scratch_check_status.
 //   * All calls on a device share the one array, which keeps the previous
 //     call's contents.  Calls whose work overlaps on the GPU (different
 //     streams, or different host threads) race on it: serialise them.
@@ -25,6 +29,7 @@
 #include <mutex>
 
 #include "b2d_decode.h"
+#include "common.cuh"
 #include "host_common.h"
 
 namespace b2d {
@@ -49,8 +54,8 @@ static int static_scratch_address(void** out) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || p == nullptr)
       return B2D_ERR_CUDA;
-    // The status word at the head of the workspace must start at zero.
-    if (cudaMemset(p, 0, 256) != cudaSuccess) return B2D_ERR_CUDA;
+    // The workspace header (status word, merge counters) must start at zero.
+    if (cudaMemset(p, 0, kWsHeaderBytes) != cudaSuccess) return B2D_ERR_CUDA;
     if (cudaDeviceSynchronize() != cudaSuccess) return B2D_ERR_CUDA;
     g_scratch_ptr[dev] = p;
   }
@@ -73,4 +78,17 @@ extern "C" int b2d_decode_gqa_static_scratch(const b2d_gqa_args* args, void* str
   a.workspace = scratch;
   a.workspace_bytes = b2d::kStaticScratchBytes;
   return b2d_decode_gqa(&a, stream);
+}
+
+extern "C" int b2d_static_scratch_check_status(int clear, void* stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B2D_ERR_CUDA;
+  if (dev < 0 || dev >= b2d::kMaxDevices) return B2D_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> g(b2d::g_scratch_mu);
+    scratch = b2d::g_scratch_ptr[dev];
+  }
+  if (scratch == nullptr) return B2D_OK;  // no call has used the array on this device
+  return b2d_check_device_status(scratch, clear, stream);
 }

@@ -20,6 +20,9 @@ static int mla_validate(const b2d_mla_args* a, bool need_pointers) {
   if (a->num_heads != 128 || a->head_dim_qk != 576 || a->head_dim_v != 512) return B2D_ERR_UNSUPPORTED;
   if (a->dtype != B2D_BF16) return B2D_ERR_UNSUPPORTED;
   if (a->page_size % mla::kT != 0) return B2D_ERR_UNSUPPORTED;
+  // Token positions (max_pages_per_seq * page_size) are 32-bit in the kernel.
+  if ((int64_t)a->max_pages_per_seq * a->page_size > (int64_t)INT32_MAX) return B2D_ERR_TOO_LARGE;
+  if (a->wait_limit_us < 0) return B2D_ERR_INVALID_ARG;
   if (!need_pointers || a->batch == 0) return B2D_OK;
   if (!a->q || !a->kv_cache || !a->cache_seqlens || !a->block_table || !a->out)
     return B2D_ERR_INVALID_ARG;
@@ -44,7 +47,7 @@ static int mla_make_plan(const b2d_mla_args* a, MlaPlan* pl) {
   pl->seqs_per_launch = a->batch < kMlaMaxRows ? (a->batch > 0 ? a->batch : 1) : kMlaMaxRows;
   pl->smem = 1024 + mla::kOffRows + (size_t)(pl->seqs_per_launch + 1) * 4 + 32 * 4;
   const size_t segs = (size_t)pl->seqs_per_launch + nr;
-  pl->off_rows = 256;
+  pl->off_rows = kWsHeaderBytes;
   pl->off_part_lse = align_up(pl->off_rows + (size_t)(pl->seqs_per_launch + 1) * 4, 256);
   pl->off_part_o = align_up(pl->off_part_lse + segs * 128 * 4, 256);
   pl->ws_bytes = align_up(pl->off_part_o + segs * 128 * 512 * 4, 256);
@@ -106,6 +109,7 @@ extern "C" int b2d_decode_mla(const b2d_mla_args* a, void* stream) {
     p.lse = a->lse ? a->lse + (size_t)b0 * a->lse_stride_b : nullptr;
     p.lse_sb = a->lse_stride_b;
     p.status = reinterpret_cast<int*>(ws);
+    p.wait_ns = a->wait_limit_us > 0 ? (unsigned long long)a->wait_limit_us * 1000ull : kWaitLimitNs;
     p.row_start_g = reinterpret_cast<int32_t*>(ws + pl.off_rows);
     p.part_lse = reinterpret_cast<float*>(ws + pl.off_part_lse);
     p.part_o = reinterpret_cast<float*>(ws + pl.off_part_o);

@@ -57,6 +57,7 @@ struct MlaParams {
   float* part_lse;           // [(B + NR) * 128], log2 units
   int32_t* row_start_g;      // [B + 1]
   int* status;
+  unsigned long long wait_ns;  // bounded-wait limit of every mbarrier wait
   int B, P, num_pages, max_pages;
   float scale_log2;
 };
@@ -169,8 +170,9 @@ __device__ __forceinline__ bool softmax_group_any(bool pred) {
 }
 
 // Wait helper that records a timeout; returns false when the kernel must stop.
-__device__ __forceinline__ bool mla_wait(uint64_t* bar, uint32_t parity, int* status) {
-  if (mbar_wait(bar, parity)) return true;
+__device__ __forceinline__ bool mla_wait(uint64_t* bar, uint32_t parity, int* status,
+                                         unsigned long long limit_ns) {
+  if (mbar_wait(bar, parity, limit_ns)) return true;
   record_status(status, kStatusTimeout);
   return false;
 }
@@ -326,7 +328,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           const int pga = __ldg(p.block_table + (int64_t)ra * p.bt_stride + pa);
           if (pga >= 0 && pga < p.num_pages) tma_prefetch_5d(&tmap_kv, ta - pa * p.P, 0, pga, 0);
         }
-        if (!mla_wait(kv_empty + s, ph ^ 1u, p.status)) break;
+        if (!mla_wait(kv_empty + s, ph ^ 1u, p.status, p.wait_ns)) break;
         mbar_arrive_expect_tx(kv_full + s, kStageBytes);
         tma_load_5d(smem + kOffKV + s * kStageBytes, &tmap_kv, kv_full + s, tok0 - pidx * p.P, 0,
                     pg, 0, policy);
@@ -348,9 +350,9 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       auto issue_pv = [&](int j, int stage, bool first_of_row) -> bool {
-        if (!mla_wait(p_full, (uint32_t)(j & 1), p.status)) return false;
+        if (!mla_wait(p_full, (uint32_t)(j & 1), p.status, p.wait_ns)) return false;
         if (first_of_row && nrow > 1) {
-          if (!mla_wait(o_empty, (uint32_t)((nrow - 2) & 1), p.status)) return false;
+          if (!mla_wait(o_empty, (uint32_t)((nrow - 2) & 1), p.status, p.wait_ns)) return false;
         }
         tc_fence_after();
         if (lane == 0) {
@@ -390,10 +392,10 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
           if (cur >= 0 && !(ok = drain_row())) break;
           cur = row;
           ++nrow;
-          if (!mla_wait(q_full, (uint32_t)(nq & 1), p.status)) { ok = false; break; }
+          if (!mla_wait(q_full, (uint32_t)(nq & 1), p.status, p.wait_ns)) { ok = false; break; }
           ++nq;
         }
-        if (!mla_wait(kv_full + s, ph, p.status)) { ok = false; break; }
+        if (!mla_wait(kv_full + s, ph, p.status, p.wait_ns)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
           const uint32_t ts = tmem + (uint32_t)((i % kSBuf) * kT);
@@ -479,7 +481,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         const int nvalid = min(kT, L - tok0);
         const int stage = i % kStages;
 
-        if (!mla_wait(s_full + i % kSBuf, (uint32_t)((i / kSBuf) & 1), p.status)) { ok = false; break; }
+        if (!mla_wait(s_full + i % kSBuf, (uint32_t)((i / kSBuf) & 1), p.status, p.wait_ns)) { ok = false; break; }
         tc_fence_after();
         // Scores of heads a and b, tokens 8j + cq + {0, 1} (j = 0..7).
         float sa[16], sb[16];
@@ -526,7 +528,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
         // P.V of the previous chunk must be complete before O is rescaled or
         // the P tile is rewritten.
         if (i > 0) {
-          if (!mla_wait(pv_done, (uint32_t)((i - 1) & 1), p.status)) { ok = false; break; }
+          if (!mla_wait(pv_done, (uint32_t)((i - 1) & 1), p.status, p.wait_ns)) { ok = false; break; }
           tc_fence_after();
         }
         if (any_need && !first_chunk) {
@@ -589,7 +591,7 @@ __global__ void __launch_bounds__(mla::kThreads, 1)
             lt_a += __shfl_xor_sync(0xffffffffu, lt_a, o);
             lt_b += __shfl_xor_sync(0xffffffffu, lt_b, o);
           }
-          if (!mla_wait(o_full, (uint32_t)((nrow - 1) & 1), p.status)) { ok = false; break; }
+          if (!mla_wait(o_full, (uint32_t)((nrow - 1) & 1), p.status, p.wait_ns)) { ok = false; break; }
           tc_fence_after();
           const int cf = cta_of_chunk(row_start[row], W, G);
           const int cl = cta_of_chunk(row_start[row + 1] - 1, W, G);

@@ -7,7 +7,7 @@ import torch
 
 import b200decode
 from b200decode import workloads as W
-from helpers import assert_parity, to_oracle
+from helpers import assert_parity, oracle_mla_streamed, to_oracle
 from oracle import decode_ref as R
 
 pytestmark = pytest.mark.gpu
@@ -83,11 +83,10 @@ def test_mla_large_scores_trigger_rescale(cuda):
 
 
 def test_mla_cfg4_full(cuda):
+    """Config 4 at full size: every sequence and head against the oracle."""
     x = _inputs(cuda, W.CFG4_MLA)
     out, lse = _run(x)
-    rows = np.array([0, 31, 64, 127])
-    ro, rl = _oracle(x, rows=rows)
-    assert_parity(out, lse, ro, rl, rows=rows)
+    assert_parity(out, lse, *oracle_mla_streamed(x))
 
 
 def test_mla_batch_larger_than_one_launch(cuda):

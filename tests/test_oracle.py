@@ -151,3 +151,19 @@ def test_e4m3_rounding_corners():
     assert not (R.f64_to_e4m3_bits(mids) & 1).any()
     sat = R.f64_to_e4m3_bits(np.array([448.0, 449.0, 1e4, -1e4]))
     np.testing.assert_array_equal(R.e4m3_bits_to_f64(sat), [448.0, 448.0, 448.0, -448.0])
+
+
+def test_streamed_oracle_matches_whole_cache_oracle():
+    """The chunked oracle used on full-size caches (only the pages a chunk of
+    sequences uses, renumbered) gives the same result as the oracle over the
+    whole cache, including a zero-length sequence."""
+    import torch
+    from b200decode import workloads as W
+    from helpers import oracle_gqa, oracle_gqa_streamed
+    w = W.CFG5_FP8.scaled(batch=7, seqlen_lo=0, seqlen_hi=300, seed=4)
+    sl = torch.tensor([0, 1, 16, 17, 299, 150, 3])
+    x = W.make_gqa_inputs(w, "cpu", seqlens=sl)
+    o1, l1 = oracle_gqa(x)
+    o2, l2 = oracle_gqa_streamed(x, chunk=3)
+    np.testing.assert_array_equal(o1, o2)
+    np.testing.assert_array_equal(l1, l2)

@@ -1,5 +1,6 @@
 """Host logic: seeded workloads, block tables, byte accounting, sharding
 (including a world-size-2 gloo all-gather on CPU)."""
+import datetime
 import os
 import socket
 
@@ -71,14 +72,23 @@ def _free_port():
 
 def _gather_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
     try:
         b, hq, d = 3, 8, 4
         full = torch.arange(b * hq * d, dtype=torch.float32).view(b, hq, d)
         lse_full = torch.arange(b * hq, dtype=torch.float32).view(b, hq)
         qs, _ = shard.head_shard(hq, 4, world, rank)
         out, lse = shard.gather_heads(full[:, qs].contiguous(), lse_full[:, qs].contiguous())
-        q.put((rank, bool(torch.equal(out, full) and torch.equal(lse, lse_full))))
+        ok = bool(torch.equal(out, full) and torch.equal(lse, lse_full))
+        # the preallocated packed form, twice (buffers are reused per step)
+        hg = shard.HeadGather(b, hq // world, d, torch.float32, "cpu")
+        for k in range(2):
+            hg.out_local.copy_(full[:, qs] + k)
+            hg.lse_local.copy_(lse_full[:, qs] - k)
+            out, lse = hg.gather()
+            ok = ok and bool(torch.equal(out, full + k) and torch.equal(lse, lse_full - k))
+        q.put((rank, ok))
     finally:
         dist.destroy_process_group()
 
@@ -134,3 +144,15 @@ def test_decodebench_mla_cli_defaults_match_reference_flags():
                                 "--num-kv-heads", "8", "--head-dim", "128", "--kv-dtype", "bf16",
                                 "--page-size", "16", "--output", "y.json", "--kv-layout", "vllm"])
     assert g.kv_layout == "vllm"
+
+
+def test_fp8_cache_generation_saturates_instead_of_nan():
+    """Config-5 style FP8 caches (scales down to 0.01, so N(0,1)/scale can
+    exceed 448) hold no e4m3 NaN code: values are saturated like a quantiser."""
+    from b200decode import workloads as W
+    w = W.CFG5_FP8.scaled(batch=8, seqlen_lo=2000, seqlen_hi=4000, kv_scale_range=(0.01, 0.011))
+    x = W.make_gqa_inputs(w, "cpu")
+    for c in (x["k_cache"], x["v_cache"]):
+        bits = c.view(torch.uint8)
+        assert int(((bits & 0x7F) == 0x7F).sum()) == 0
+        assert int(((bits & 0x7F) == 0x7E).sum()) > 0   # some values did saturate to 448

@@ -53,6 +53,29 @@ def test_static_scratch_matches_regular_entry_point(cuda):
         torch.cuda.synchronize()
         assert _close(out, ref_out, OUT_ATOL, OUT_RTOL)
         assert _close(lse, ref_lse, LSE_ATOL, 0.0)
+        # nothing went wrong on the device during the call
+        assert lib.b2d_static_scratch_check_status(1, stream) == 0
+
+
+def test_static_scratch_reports_device_errors(cuda):
+    """A block-table entry out of range is clamped to page 0 by the kernel
+    and recorded in the scratch array's status word; the static-scratch
+    status call reports it once, clears it, and the next call is clean."""
+    lib = _lib.load()
+    stream = C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    x = W.make_gqa_inputs(W.CFG2_GQA_PAGED.scaled(batch=4, seqlen_lo=40, seqlen_hi=200, seed=13),
+                          cuda)
+    out = torch.empty_like(x["q"])
+    lse = torch.empty(x["q"].shape[:2], dtype=torch.float32, device=cuda)
+    good = x["block_table"].clone()
+    x["block_table"][1, 0] = x["k_cache"].shape[0] + 5
+    a = _args_for(x, out, lse)
+    assert lib.b2d_decode_gqa_static_scratch(C.byref(a), stream) == 0
+    assert lib.b2d_static_scratch_check_status(1, stream) == -7   # B2D_ERR_DEVICE_BOUNDS
+    assert lib.b2d_static_scratch_check_status(1, stream) == 0    # cleared
+    x["block_table"].copy_(good)
+    assert lib.b2d_decode_gqa_static_scratch(C.byref(a), stream) == 0
+    assert lib.b2d_static_scratch_check_status(1, stream) == 0
 
 
 def test_static_scratch_rejects_too_large(cuda):
