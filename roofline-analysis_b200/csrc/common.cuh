@@ -82,6 +82,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   return true;
 }
 
+// Programmatic dependent launch.  A kernel launched with the
+// programmatic-stream-serialization attribute may start while the previous
+// kernel on the stream is still finishing; griddep_wait() blocks until that
+// kernel has completed and its memory is visible, so it must come before
+// the first read of any input or write of any output.  griddep_launch()
+// lets the next such kernel start its own prologue early.  Both are no-ops
+// for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
@@ -151,6 +165,17 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2_cvt(uint32_t w) {
       : "=r"(r)
       : "r"(w));
   return r;
+}
+
+// atomicAdd with release + acquire semantics at GPU scope: writes this
+// thread made before it (and, after a __syncwarp(), those of its warp) are
+// visible to whoever observes the new value, and writes that the previous
+// releasers made are visible to this thread afterwards.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v)
+               : "memory");
+  return old;
 }
 
 __device__ __forceinline__ void record_status(int* status, int bits) {

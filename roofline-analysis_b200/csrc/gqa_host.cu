@@ -221,7 +221,22 @@ static int launch_k(Kern kern, void (*combine)(const GqaParams, int, int), const
   if (!(flags & B2D_FLAG_COMBINE_ONLY)) {
     GqaParams pk = p;
     pk.merge_count = fused ? p.merge_count : nullptr;
-    kern<<<ctas, threads, pl.smem, st>>>(tk, tv, pk);
+    // Programmatic dependent launch (B2D_PDL=0 turns it off): the kernel's
+    // prologue (barrier set-up, descriptor prefetch) overlaps the tail of
+    // the previous kernel on the stream; the kernel waits for that kernel's
+    // completion before it reads any input.
+    static const int pdl = env_int("B2D_PDL", 1);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, tk, tv, pk) != cudaSuccess) return B2D_ERR_CUDA;
     if (cudaGetLastError() != cudaSuccess) return B2D_ERR_CUDA;
   }
   if (fused) return B2D_OK;

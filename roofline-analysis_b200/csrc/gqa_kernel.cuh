@@ -231,6 +231,10 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
   }
+  // Everything above touches only shared memory and kernel parameters: with
+  // programmatic dependent launch it overlaps the previous kernel's tail.
+  griddep_wait();
+  griddep_launch();
   build_row_start(p, R, row_start, warp_tmp);  // ends with __syncthreads
   if (cta == 0) {
     for (int i = threadIdx.x; i <= R; i += blockDim.x) p.row_start_g[i] = row_start[i];
@@ -539,25 +543,28 @@ __global__ void __maxnreg__(B2D_GQA_MAXNREG)
 // One warp merges the split partials of query heads [qh_row0, qh_row0 + nh)
 // of row (b, hg) over segments seg0 .. seg0 + nseg - 1 (the LSE rule of
 // cluster_decode_reduce.py:67-91 in log2 units) and writes out and lse.
-// Used by the split-KV kernel's last-arriving warp (the partials of other
-// CTAs are read past L1, after the acquire fence of the arrival counter).
+// Used by the split-KV kernel's last-arriving warp, at the very end of the
+// kernel, so it is pure latency: two heads are merged at once (half a warp
+// each, 2 * D / 32 elements per lane) and every segment's lse and partial
+// output of a batch of U segments are loaded together, folded in with a
+// running maximum.  The partials of other CTAs are read past L1 (__ldcg),
+// after the acquire fence of the arrival counter.
 template <int D, typename QT>
 __device__ __forceinline__ void warp_merge_heads(const GqaParams& p, int b, int hg, int HQC,
                                                  int qh_row0, int nh, int64_t seg0, int nseg) {
   constexpr float kLn2 = 0.69314718055994530942f;
-  constexpr int EPL = D / 32;
-  constexpr int U = D >= 256 ? 4 : 8;
+  constexpr int EPL = D / 16;              // elements per lane (half a warp per head)
+  constexpr int U = D <= 128 ? 8 : 4;      // segments per load batch
   const int lane = threadIdx.x & 31;
-  for (int hw = 0; hw < nh; ++hw) {
-    const int qh_row = qh_row0 + hw;
-    float mx = -INFINITY;
-    for (int j = lane; j < nseg; j += 32) mx = fmaxf(mx, __ldcg(p.part_lse + (seg0 + j) * HQC + qh_row));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int half = lane >> 4, hl = lane & 15;
+  for (int hw0 = 0; hw0 < nh; hw0 += 2) {
+    const int hw = hw0 + half;
+    const bool live = hw < nh;
+    const int qh_row = qh_row0 + (live ? hw : hw0);
     float acc[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-    float wsum = 0.f;
+    float wsum = 0.f, mx = -INFINITY;
     for (int j0 = 0; j0 < nseg; j0 += U) {
       float lv[U];
       float2 v[U][EPL / 2];
@@ -565,10 +572,20 @@ __device__ __forceinline__ void warp_merge_heads(const GqaParams& p, int b, int 
       for (int u = 0; u < U; ++u) {
         const int j = j0 + u < nseg ? j0 + u : nseg - 1;
         lv[u] = __ldcg(p.part_lse + (seg0 + j) * HQC + qh_row);
-        const float2* src = reinterpret_cast<const float2*>(p.part_o + ((seg0 + j) * HQC + qh_row) * D + lane * EPL);
+        const float2* src = reinterpret_cast<const float2*>(
+            p.part_o + ((seg0 + j) * HQC + qh_row) * D + hl * EPL);
 #pragma unroll
         for (int e = 0; e < EPL / 2; ++e) v[u][e] = __ldcg(src + e);
       }
+      float bm = mx;
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (j0 + u < nseg) bm = fmaxf(bm, lv[u]);
+      const float r = (mx == -INFINITY) ? 0.f : fast_exp2(mx - bm);
+      wsum *= r;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[e] *= r;
+      mx = bm;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const float w = (j0 + u < nseg) ? fast_exp2(lv[u] - mx) : 0.f;
@@ -580,12 +597,14 @@ __device__ __forceinline__ void warp_merge_heads(const GqaParams& p, int b, int 
         }
       }
     }
-    const int qh = hg * HQC + qh_row;
-    QT* dst = reinterpret_cast<QT*>(p.out) + (int64_t)b * p.o_sb + (int64_t)qh * p.o_sh + lane * EPL;
-    const float inv = 1.f / wsum;
+    if (live) {
+      const int qh = hg * HQC + qh_row;
+      QT* dst = reinterpret_cast<QT*>(p.out) + (int64_t)b * p.o_sb + (int64_t)qh * p.o_sh + hl * EPL;
+      const float inv = 1.f / wsum;
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) dst[e] = QT(acc[e] * inv);
-    if (p.lse != nullptr && lane == 0) p.lse[(int64_t)b * p.lse_sb + qh] = (mx + fast_log2(wsum)) * kLn2;
+      for (int e = 0; e < EPL; ++e) dst[e] = QT(acc[e] * inv);
+      if (p.lse != nullptr && hl == 0) p.lse[(int64_t)b * p.lse_sb + qh] = (mx + fast_log2(wsum)) * kLn2;
+    }
   }
 }
 

@@ -171,6 +171,10 @@ __global__ void __launch_bounds__(32 * 9, 1)
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
   }
+  // Everything above touches only shared memory and kernel parameters: with
+  // programmatic dependent launch it overlaps the previous kernel's tail.
+  griddep_wait();
+  griddep_launch();
   build_row_start(p, R, row_start, warp_tmp);
   if (cta == 0) {
     for (int i = threadIdx.x; i <= R; i += blockDim.x) p.row_start_g[i] = row_start[i];
@@ -357,17 +361,17 @@ __global__ void __launch_bounds__(32 * 9, 1)
     (void)kvh;
     if (cf != cl && p.merge_count != nullptr) {
       // In-kernel merge: every warp that wrote a partial of these heads
-      // counts itself in (release: fence, then the atomic); the warp that
-      // arrives last (acquire: the atomic, then a fence) merges all
-      // cl - cf + 1 partials and re-arms the counter for the next call.
-      __threadfence();
+      // counts itself in with one acquire-release atomic (the __syncwarp
+      // orders the other lanes' partial stores before lane 0's release);
+      // the warp that arrives last has acquired every other partial, merges
+      // all cl - cf + 1 of them and re-arms the counter for the next call.
       __syncwarp();
       int* cnt = p.merge_count + (int64_t)row * p.NW + warp;
       int old = 0;
-      if (lane == 0) old = atomicAdd(cnt, 1);
+      if (lane == 0) old = atomic_add_acq_rel_gpu(cnt, 1);
       old = __shfl_sync(0xffffffffu, old, 0);
       if (old == cl - cf) {
-        __threadfence();
+        __syncwarp();   // lane 0's acquire, then the other lanes' loads
         warp_merge_heads<D, QT>(p, b, hg, HQC, qh_row0, GW, (int64_t)row + cf, cl - cf + 1);
         if (lane == 0) *cnt = 0;
       }
