@@ -218,6 +218,14 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--kv-scale-range", type=float, nargs=2, default=None, metavar=("LO", "HI"),
                     help="fp8 only: per-KV-head dequantisation scales ~ U[LO, HI] "
                          "(default: unit scales, as the reference)")
+    ap.add_argument("--ncu", action="store_true",
+                    help="re-run once under Nsight Compute and merge DRAM bytes, traffic ratio "
+                         "and tensor-pipe utilisation of the split-KV kernel into the record "
+                         "(small cases only)")
+    ap.add_argument("--num-gpus", type=int, default=1,
+                    help="shard the batch (--shard dp) or the KV heads (--shard tp) over this "
+                         "many GPUs, one process each (NCCL)")
+    ap.add_argument("--shard", choices=["dp", "tp"], default="dp")
     ap.add_argument("--kv-layout", default="NHD", choices=["NHD", "HND", "vllm"],
                     help="cache layout handed to the kernel (vllm = paged_attention's "
                          "K [blocks, Hkv, D/8, P, 8], V [blocks, Hkv, D, P])")
@@ -243,10 +251,21 @@ def parse_mla_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--seqlen-hi", type=int, default=None)
     ap.add_argument("--page-perm", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--ncu", action="store_true",
+                    help="re-run once under Nsight Compute and merge the MLA kernel's counters "
+                         "into the record (small cases only)")
     return ap.parse_args(argv)
 
 
+def _child_argv(argv, mla: bool):
+    """The same adapter command without --ncu (what ncu re-runs)."""
+    a = [x for x in argv if x != "--ncu"]
+    return (["mla"] if mla else []) + a
+
+
 def main_mla(argv=None) -> int:
+    import sys
+    argv = sys.argv[2:] if argv is None else list(argv)
     args = parse_mla_args(argv)
     shape = MlaDecodeShape(args.batch_size, args.context_len, args.num_q_heads,
                            args.num_kv_heads, args.qk_nope_head_dim, args.kv_lora_rank,
@@ -291,6 +310,10 @@ def main_mla(argv=None) -> int:
         "seed": args.seed,
         "page_perm": args.page_perm,
     }
+    if args.ncu:
+        from . import ncu_harness
+        result["ncu"] = ncu_harness.capture(_child_argv(argv, True), "mla", skip=args.warmup_steps,
+                                            count=min(3, args.repeat), algorithmic_bytes=alg)
     args.output.parent.mkdir(parents=True, exist_ok=True)
     args.output.write_text(json.dumps(result, indent=2) + "\n", encoding="utf-8")
     print(json.dumps(result))
@@ -305,6 +328,8 @@ def main(argv=None) -> int:
     args = parse_args(argv)
     shape = DecodeShape(args.batch_size, args.context_len, args.num_q_heads, args.num_kv_heads,
                         args.head_dim, args.kv_dtype, args.page_size)
+    if args.num_gpus > 1:
+        return main_multi_gpu(args, shape)
     kernel = B2DDecodeKernel(shape, args.seqlen_lo, args.seqlen_hi, args.page_perm, args.seed,
                              kv_scale_range=(tuple(args.kv_scale_range) if args.kv_scale_range
                                              else None),
@@ -352,6 +377,135 @@ def main(argv=None) -> int:
         "cuda_graph": args.cuda_graph,
         "kv_layout": args.kv_layout,
         "kv_scale_range": args.kv_scale_range,
+    }
+    if args.ncu:
+        from . import ncu_harness
+        # -k selects the split-KV kernel: one launch per run, plus the one
+        # run that records the CUDA graph
+        result["ncu"] = ncu_harness.capture(_child_argv(argv, False), "gqa",
+                                            skip=args.warmup_steps + (1 if args.cuda_graph else 0),
+                                            count=min(3, args.repeat), algorithmic_bytes=alg)
+    args.output.parent.mkdir(parents=True, exist_ok=True)
+    args.output.write_text(json.dumps(result, indent=2) + "\n", encoding="utf-8")
+    print(json.dumps(result))
+    return 0
+
+
+def _mg_worker(rank: int, world: int, port: int, args, shape: DecodeShape, q):
+    """One rank of a sharded decodebench run: build the whole batch (same
+    seed on every rank), keep this rank's shard, time its decode (plus the
+    head all-gather under TP) with one CUDA-event pair per run, and send the
+    p50 and the shard's bytes to rank 0."""
+    import datetime as _dt
+    import torch.distributed as dist
+    from . import shard
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=_dt.timedelta(seconds=120))
+    try:
+        k = B2DDecodeKernel(shape, args.seqlen_lo, args.seqlen_hi, args.page_perm, args.seed,
+                            kv_scale_range=(tuple(args.kv_scale_range) if args.kv_scale_range
+                                            else None))
+        x, w = k.x, k.workload
+        if args.shard == "dp":
+            rows = shard.balance_sequences(x["cache_seqlens"].tolist(), world)[rank]
+            y = shard.slice_gqa_inputs_by_batch(x, rows, seed=args.seed + rank)
+            wl = w.scaled(batch=len(rows))
+            hg = None
+        else:
+            y = shard.slice_gqa_inputs_by_heads(x, world, rank)
+            wl = w.scaled(num_q_heads=w.num_q_heads // world, num_kv_heads=w.num_kv_heads // world)
+            hg = shard.HeadGather(w.batch, wl.num_q_heads, w.head_dim, x["q"].dtype, dev)
+        del k, x
+        dec = api.GqaDecoder(y["q"], y["k_cache"], y["v_cache"], y["cache_seqlens"],
+                             y["block_table"], y["softmax_scale"], k_scale=y["k_scale"],
+                             v_scale=y["v_scale"], out=None if hg is None else hg.out_local,
+                             lse=None if hg is None else hg.lse_local)
+
+        def step():
+            dec.run()
+            if hg is not None:
+                hg.gather()
+
+        for _ in range(args.warmup_steps):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        times = cuda_time_ms(step, args.repeat)
+        sl = y["cache_seqlens"].cpu()
+        mine = {"rank": rank, "p50_ms": percentile(times, 50), "p95_ms": percentile(times, 95),
+                "kv_bytes": W.gqa_kv_bytes_reference(wl, sl),
+                "alg_bytes": W.gqa_algorithmic_bytes(wl, sl), "sequences": int(sl.numel()),
+                "tokens": int(sl.sum())}
+        allr = [None] * world
+        dist.all_gather_object(allr, mine)
+        if rank == 0:
+            q.put(allr)
+    finally:
+        dist.destroy_process_group()
+
+
+def main_multi_gpu(args, shape: DecodeShape) -> int:
+    """--num-gpus N: one process per GPU (NCCL), batch- or head-sharded; the
+    record's latency is the slowest rank's p50 and its bandwidth is all
+    ranks' bytes over that latency."""
+    import socket
+    import torch.multiprocessing as mp
+    world = args.num_gpus
+    if torch.cuda.device_count() < world:
+        raise RuntimeError(f"--num-gpus {world} needs {world} GPUs, found {torch.cuda.device_count()}")
+    if args.shard == "tp" and shape.num_kv_heads % world:
+        raise ValueError("--shard tp needs num_kv_heads divisible by --num-gpus")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_mg_worker, args=(r, world, port, args, shape, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    ranks = q.get(timeout=900)
+    for p in procs:
+        p.join(120)
+    worst = max(ranks, key=lambda r: r["p50_ms"])
+    kv = sum(r["kv_bytes"] for r in ranks)
+    alg = sum(r["alg_bytes"] for r in ranks)
+    result = {
+        "run_id": os.environ.get("DECODEBENCH_RUN_ID"),
+        "timestamp": datetime.now(timezone.utc).isoformat(),
+        "gpu": torch.cuda.get_device_name(),
+        "backend": "b2d_decode",
+        "kernel_path": f"b2d gqa_mma_kernel (sm_100a) via libb2d.so, {args.shard}{world}",
+        "layer": "kernel",
+        "workload_id": os.environ.get("DECODEBENCH_WORKLOAD_ID"),
+        "attention": shape.attention,
+        "kv_dtype": shape.kv_dtype,
+        "page_size": shape.page_size,
+        "batch_size": shape.batch_size,
+        "context_len": shape.context_len,
+        "decode_steps": 1,
+        "num_gpus": world,
+        "shard": args.shard,
+        "compare_latency_us": worst["p50_ms"] * 1000.0,
+        "kernel_latency_p50_us": worst["p50_ms"] * 1000.0,
+        "kernel_latency_p95_us": max(r["p95_ms"] for r in ranks) * 1000.0,
+        "approx_kv_bytes_read": kv,
+        "approx_effective_kv_bandwidth_gb_s": kv / (worst["p50_ms"] * 1e6),
+        "fallback": False,
+        "fallback_reason": None,
+        "notes": ("one process per GPU over NCCL; latency = slowest rank's p50"
+                  + ("; TP step includes the packed out/lse all-gather" if args.shard == "tp" else "")),
+        "roofline_bytes": alg,
+        "achieved_tb_s": alg / (worst["p50_ms"] * 1e-3) / 1e12,
+        "per_rank": ranks,
+        "seqlen_lo": args.seqlen_lo,
+        "seqlen_hi": args.seqlen_hi,
+        "seed": args.seed,
+        "page_perm": args.page_perm,
     }
     args.output.parent.mkdir(parents=True, exist_ok=True)
     args.output.write_text(json.dumps(result, indent=2) + "\n", encoding="utf-8")
