@@ -63,6 +63,10 @@ def parse_args():
                     help="CPU work budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sustained-s", type=float, default=1.0,
+                    help="seconds of the extra sustained loop (power-capped steady state)")
+    ap.add_argument("--no-other-workloads", action="store_true",
+                    help="skip the short cfg2 / cfg4 lines that an N=1 cfg5 run adds")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch (smaller profiling cases)")
     return ap.parse_args()
@@ -80,14 +84,20 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def committed_traffic(workload: str):
-    """Per-launch DRAM bytes of the split-KV kernel from the committed ncu
-    summary (profiles/traffic.json), or None."""
+def committed_traffic(workload: str, bytes_per_launch: int):
+    """(traffic, tensor_pipe_pct, source) of the split-KV kernel from the
+    committed ncu records (profiles/traffic.json, written from `decodebench
+    --ncu` captures): the captured case's DRAM / algorithmic ratio times this
+    launch's algorithmic bytes."""
     try:
-        d = json.loads((REPO / "profiles" / "traffic.json").read_text())
-        return d.get(workload)
+        d = json.loads((REPO / "profiles" / "traffic.json").read_text()).get(workload)
     except Exception:
-        return None
+        d = None
+    if not d or not d.get("traffic_ratio"):
+        return None, None, None
+    ratio = d["traffic_ratio"]
+    return (int(ratio * bytes_per_launch), d.get("tensor_pipe_pct"),
+            f"ncu capture ({d.get('captured', '')}), DRAM/algorithmic {ratio:.4f} scaled to this launch")
 
 
 class ClockSampler:
@@ -149,6 +159,32 @@ class ClockSampler:
 def dist_setup():
     return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
             int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def other_workloads(args):
+    """At N=1, short lines of the other BASELINE GPU configurations (GQA bf16
+    config 2 and MLA config 4), each from its own bench.py process, so one
+    driver run also times MLA."""
+    if args.no_other_workloads or args.workload not in ("cfg5", "cfg5_fp8_b256_p16") or args.batch:
+        return None
+    import subprocess
+    res = {}
+    for wl in ("cfg2", "cfg4"):
+        cmd = [sys.executable, str(REPO / "bench.py"), "--workload", wl, "--steps", str(args.steps),
+               "--warmup", str(max(3, args.warmup)), "--no-cpu-baseline", "--no-e2e",
+               "--no-other-workloads", "--sustained-s", "0.2"]
+        try:
+            out = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+            d = json.loads(out.stdout.strip().splitlines()[-1])
+            r = d["roofline"]
+            res[wl] = {"workload": d["config"]["workload"], "us_per_step": d["us_per_step"],
+                       "value": d["value"], "unit": d["unit"], "roofline_bound": r["bound"],
+                       "kernel_achieved": r["achieved"], "frac": r["frac"],
+                       "tensor": r.get("tensor"), "sustained_us_per_step": d["sustained"]["us_per_step"],
+                       "clocks": d["clocks"]}
+        except Exception as e:
+            res[wl] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    return res
 
 
 def gather_rows(vals, world: int, device):
@@ -354,7 +390,26 @@ def main():
     combine_ms = timed(_lib.B2D_FLAG_COMBINE_ONLY, kk) if launches_per_step > 1 else 0.0
     sampler_k.__exit__()
     peak, peak_kind = measured_hbm_peak()
-    achieved_gbs = local_bytes / (kern_ms * 1e-3) / 1e9
+    # When a step is one launch of the split-KV kernel (merge in-kernel, no
+    # collective), the timed region itself times that kernel: its per-step
+    # time is the launch duration plus the gap to the next launch.
+    roof_from_step = launches_per_step == 1 and not tp
+    roof_ms = local_ms if roof_from_step else kern_ms
+    achieved_gbs = local_bytes / (roof_ms * 1e-3) / 1e9
+
+    # ---- sustained: the same step for about a second, under the power cap ----
+    sus_steps = max(args.steps, int(math.ceil(args.sustained_s * 1e3 / max(local_ms, 1e-3))))
+    sampler_s = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with sampler_s:
+        ev0.record(stream)
+        for _ in range(sus_steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    sus_ms = reduce_over_ranks(ev0.elapsed_time(ev1) / sus_steps, world, dev, MAX)
 
     # ---- end to end through the public API with host buffers ----
     e2e = None
@@ -471,7 +526,11 @@ def main():
                              w0.kv_dtype == "fp8" and w0.head_dim < 128) else "b2d::gqa_decode_kernel",
                          "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved_gbs / peak, 4), "peak_source": peak_kind,
-                         "traffic": committed_traffic(w0.name),
+                         "timed_from": ("the timed region (one launch per step)" if roof_from_step
+                                        else "a loop of the split-KV kernel alone"),
+                         "traffic": committed_traffic(w0.name, local_bytes)[0],
+                         "traffic_source": committed_traffic(w0.name, local_bytes)[2],
+                         "tensor_pipe_pct": committed_traffic(w0.name, local_bytes)[1],
                          "kernel_us": round(kern_ms * 1e3, 2),
                          "combine_us": round(combine_ms * 1e3, 2),
                          "cuda_graph_step_us": None if graph_ms is None else round(graph_ms * 1e3, 2),
@@ -482,6 +541,12 @@ def main():
             "launches_per_step": launches_per_step,
             "clocks": sampler.summary(),
             "clocks_kernel_loops": sampler_k.summary(),
+            "sustained": {"us_per_step": round(sus_ms * 1e3, 2), "steps": sus_steps,
+                          "value": round(total_bytes / (sus_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+                          "clocks": sampler_s.summary(),
+                          "note": "the same step repeated for about a second; the power cap "
+                                  "(sw_power_cap) lowers SM clocks after ~50-100 ms of FP8 decode"},
+            "other_workloads": other_workloads(args) if world == 1 else None,
             "per_rank": [{"rank": r, "us_per_step": round(v[0], 2), "tokens": int(v[1]),
                           "sequences": int(v[2]), "kernel_us": round(v[3], 2),
                           "cuda_graph_step_us": round(v[4], 2) if v[4] else None}
@@ -581,6 +646,17 @@ def run_mla(args, world, rank, local, w0):
 
     kern_ms = timed(_lib.B2D_FLAG_SKIP_COMBINE)
     combine_ms = timed(_lib.B2D_FLAG_COMBINE_ONLY)
+    # sustained: the same step for about a second
+    sus_steps = max(args.steps, int(math.ceil(args.sustained_s * 1e3 / max(ms, 1e-3))))
+    sampler_s = ClockSampler(local)
+    torch.cuda.synchronize()
+    with sampler_s:
+        ev0.record(stream)
+        for _ in range(sus_steps):
+            dec()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    sus_ms = reduce_over_ranks(ev0.elapsed_time(ev1) / sus_steps, world, dev, MAX)
     total_bytes = reduce_over_ranks(local_bytes, world, dev, SUM)
     total_flops = reduce_over_ranks(local_flops, world, dev, SUM)
     hbm_peak, hbm_kind = measured_hbm_peak()
@@ -695,10 +771,16 @@ def run_mla(args, world, rank, local, w0):
                          "peak_source": hbm_kind,
                          "tensor": {"achieved": round(ach_tfs, 1), "peak": tc_peak, "unit": "TFLOP/s",
                                     "frac": round(ach_tfs / tc_peak, 4), "peak_source": tc_kind},
-                         "traffic": committed_traffic(w0.name), "kernel_us": round(kern_ms * 1e3, 2),
+                         "traffic": committed_traffic(w0.name, local_bytes)[0],
+                         "traffic_source": committed_traffic(w0.name, local_bytes)[2],
+                         "tensor_pipe_pct": committed_traffic(w0.name, local_bytes)[1],
+                         "kernel_us": round(kern_ms * 1e3, 2),
                          "combine_us": round(combine_ms * 1e3, 2), "bytes_per_launch": int(local_bytes)},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
             "clocks": sampler.summary(),
+            "sustained": {"us_per_step": round(sus_ms * 1e3, 2), "steps": sus_steps,
+                          "value": round(total_bytes / (sus_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+                          "clocks": sampler_s.summary()},
         }
         print(json.dumps(line), flush=True)
     if world > 1:
