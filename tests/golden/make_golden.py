@@ -18,6 +18,12 @@ Fixtures written:
   the reference's decode call, F.scaled_dot_product_attention(..., is_causal=
   False, enable_gqa=True) (decodebench/torch_sdpa_benchmark.py:100-102), run
   in fp32 on the gathered pages; lse from torch.logsumexp of the same scores.
+* sdpa_paged_mla.npz — a small absorbed-MLA decode whose geometry comes
+  from the reference's own shape record, decodebench/trtllm_mla_kernel.py:
+  7-26 (TRTLLMMLADecodeShape: latent row = kv_lora_rank + qk_rope_head_dim
+  columns, V = the first kv_lora_rank of them, softmax scale 1/sqrt(
+  head_dim_qk) as at :77), answered by the same SDPA call with one shared
+  KV head (enable_gqa) on the gathered latent pages.
 
 Nothing under tests/ or the package imports the reference at run time; the
 tests read only the .npz files.
@@ -95,10 +101,51 @@ def sdpa_paged_fixture() -> None:
         out=np.stack(outs), lse=np.stack(lses))
 
 
+def sdpa_paged_mla_fixture(ref_root: Path) -> None:
+    sys.path.insert(0, str(ref_root / "decodebench"))
+    from trtllm_mla_kernel import TRTLLMMLADecodeShape  # noqa: E402
+
+    shape = TRTLLMMLADecodeShape(batch_size=2, context_len=70, num_q_heads=8, num_kv_heads=1,
+                                 qk_nope_head_dim=128, kv_lora_rank=512, qk_rope_head_dim=64,
+                                 kv_dtype="bf16", page_size=64)
+    width = shape.kv_lora_rank + shape.qk_rope_head_dim
+    dv = shape.kv_lora_rank
+    scale = 1.0 / (shape.head_dim_qk ** 0.5)
+    g = torch.Generator().manual_seed(7)
+    lens = [1, shape.context_len]
+    page = shape.page_size
+    npg = [(l + page - 1) // page for l in lens]
+    total = sum(npg)
+    perm = torch.randperm(total, generator=g)
+    bt = torch.zeros(shape.batch_size, max(npg), dtype=torch.int32)
+    off = 0
+    for i, n in enumerate(npg):
+        bt[i, :n] = perm[off:off + n].int()
+        off += n
+    q = (0.5 * torch.randn(shape.batch_size, shape.num_q_heads, width, generator=g)).to(torch.bfloat16)
+    kv = (0.5 * torch.randn(total, page, width, generator=g)).to(torch.bfloat16)
+    outs, lses = [], []
+    for i, l in enumerate(lens):
+        rows = kv[bt[i, :npg[i]].long()].reshape(-1, width)[:l].float()
+        k = rows[None, None]
+        v = rows[None, None, :, :dv]
+        qq = q[i:i + 1, :, None, :].float()
+        o = F.scaled_dot_product_attention(qq, k, v, is_causal=False, scale=scale, enable_gqa=True)
+        outs.append(o[0, :, 0].numpy())
+        sc = (qq[0, :, 0] @ rows.T) * scale
+        lses.append(torch.logsumexp(sc, dim=-1).numpy())
+    np.savez_compressed(
+        HERE / "sdpa_paged_mla.npz",
+        q_bits=q.view(torch.int16).numpy(), kv_bits=kv.view(torch.int16).numpy(),
+        block_table=bt.numpy(), seqlens=np.array(lens, dtype=np.int32), scale=np.float64(scale),
+        head_dim_v=np.int64(dv), out=np.stack(outs), lse=np.stack(lses))
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         sys.exit("usage: python tests/golden/make_golden.py /path/to/Roofline-Analysis")
     root = Path(sys.argv[1])
     split_merge_fixture(root)
     sdpa_paged_fixture()
+    sdpa_paged_mla_fixture(root)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))

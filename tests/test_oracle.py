@@ -43,6 +43,19 @@ def test_paged_oracle_matches_reference_sdpa_call():
     np.testing.assert_allclose(lse, z["lse"], rtol=0, atol=1e-5)
 
 
+def test_mla_oracle_matches_reference_sdpa_call():
+    """The absorbed-MLA oracle against the fixture whose geometry (576-wide
+    latent rows, V = first 512 columns, scale 1/sqrt(192)) comes from the
+    reference's TRTLLMMLADecodeShape and whose answer is its SDPA call."""
+    z = np.load(GOLD / "sdpa_paged_mla.npz")
+    q = R.bf16_bits_to_f64(z["q_bits"].view(np.uint16))
+    kv = R.bf16_bits_to_f64(z["kv_bits"].view(np.uint16))
+    out, lse = R.paged_decode_mla(q, kv, z["seqlens"], z["block_table"], float(z["scale"]),
+                                  head_dim_v=int(z["head_dim_v"]))
+    np.testing.assert_allclose(out, z["out"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(lse, z["lse"], rtol=0, atol=1e-5)
+
+
 def test_e4m3_table_matches_definition_and_torch():
     codes = np.arange(256, dtype=np.uint8)
     tab = R.e4m3_bits_to_f64(codes)
