@@ -15,8 +15,11 @@ namespace b2d {
 constexpr int kMaxRowsPerLaunch = 2048;
 // Default shared-memory budget for the K/V stage ring of one CTA.
 constexpr size_t kStageRingBytes = 96 * 1024;
-// Most resident CTAs per SM the workspace is sized for.
-constexpr int kMaxCtasPerSm = 4;
+// Most resident CTAs per SM (and the wave the workspace is sized for).  8
+// lets the small tiles of one-KV-head-per-rank tensor parallelism (2 warps
+// per CTA) reach ~6 CTAs per SM: 141 -> 100 us for a config-5 rank at TP 8;
+// B2D_GQA_MAX_CTAS_PER_SM overrides it (1..16).
+static int max_ctas_per_sm();
 
 // Tuning knobs read once from the environment (for measurement sweeps):
 // B2D_GQA_HQW caps the query heads per consumer warp (1, 2 or 4) and
@@ -24,6 +27,14 @@ constexpr int kMaxCtasPerSm = 4;
 static int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   return v ? atoi(v) : dflt;
+}
+
+static int max_ctas_per_sm() {
+  static const int v = [] {
+    const int e = env_int("B2D_GQA_MAX_CTAS_PER_SM", 8);
+    return e < 1 ? 1 : (e > 16 ? 16 : e);
+  }();
+  return v;
 }
 
 struct GqaPlan {
@@ -178,7 +189,7 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
   if (ctas <= 0) {
     int sms = 0;
     if (device_sm_count(&sms) != 0) return B2D_ERR_CUDA;
-    ctas_cap = sms * kMaxCtasPerSm;
+    ctas_cap = sms * max_ctas_per_sm();
   }
   pl->ctas = ctas;
   const int hqc = pl->hk * group;
@@ -202,7 +213,7 @@ static int launch_k(Kern kern, void (*combine)(const GqaParams, int, int), const
     if (device_sm_count(&sms) != 0) return B2D_ERR_CUDA;
     if (occupancy_per_sm(reinterpret_cast<const void*>(kern), threads, pl.smem, &per_sm))
       return B2D_ERR_CUDA;
-    per_sm = per_sm < 1 ? 1 : (per_sm > kMaxCtasPerSm ? kMaxCtasPerSm : per_sm);
+    per_sm = per_sm < 1 ? 1 : (per_sm > max_ctas_per_sm() ? max_ctas_per_sm() : per_sm);
     ctas = sms * per_sm;
   }
   const int R = p.B * p.HG;
