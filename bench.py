@@ -398,7 +398,9 @@ def main():
     achieved_gbs = local_bytes / (roof_ms * 1e-3) / 1e9
 
     # ---- sustained: the same step for about a second, under the power cap ----
-    sus_steps = max(args.steps, int(math.ceil(args.sustained_s * 1e3 / max(local_ms, 1e-3))))
+    # sized from the max-over-ranks step time, the same on every rank: under
+    # TP each step is a collective, so every rank must run the same count
+    sus_steps = max(args.steps, int(math.ceil(args.sustained_s * 1e3 / max(ms, 1e-3))))
     sampler_s = ClockSampler(local)
     if world > 1:
         dist.barrier()
