@@ -37,6 +37,9 @@ static int max_ctas_per_sm() {
   return v;
 }
 
+struct GqaPlan;
+static int plan_ctas_per_sm(const GqaPlan& pl);
+
 struct GqaPlan {
   bool mma;  // tensor-core consumer (page size % 16 == 0) or CUDA-core consumer
   int np;    // mma: PV column tiles (1: <= 8 query heads per warp, 2: <= 16)
@@ -46,6 +49,21 @@ struct GqaPlan {
   size_t off_row_start, off_part_lse, off_part_o, ws_bytes;
   int* launch_count;  // when set: count the launches a call makes, launch nothing
 };
+
+// Most CTAs of this plan that can be resident on one SM: max_ctas_per_sm(),
+// bounded by the SM's shared memory (228 KB, 1 KB reserved per CTA) and
+// threads (2048).  The workspace is sized for this many CTAs per SM and the
+// launch never uses more, so small tiles get up to 8 CTAs per SM without
+// inflating the workspace of the large ones.
+static int plan_ctas_per_sm(const GqaPlan& pl) {
+  const int threads = 32 * (pl.nw + 1);
+  int cap = max_ctas_per_sm();
+  const int by_smem = (int)(233472 / (pl.smem + 1024));
+  const int by_threads = 2048 / threads;
+  if (by_smem < cap) cap = by_smem;
+  if (by_threads < cap) cap = by_threads;
+  return cap < 1 ? 1 : cap;
+}
 
 static int kv_elem_bytes(int kv_dtype) { return kv_dtype == B2D_FP8_E4M3 ? 1 : 2; }
 
@@ -189,7 +207,7 @@ static int make_plan(const b2d_gqa_args* a, GqaPlan* pl) {
   if (ctas <= 0) {
     int sms = 0;
     if (device_sm_count(&sms) != 0) return B2D_ERR_CUDA;
-    ctas_cap = sms * max_ctas_per_sm();
+    ctas_cap = sms * plan_ctas_per_sm(*pl);
   }
   pl->ctas = ctas;
   const int hqc = pl->hk * group;
@@ -213,7 +231,8 @@ static int launch_k(Kern kern, void (*combine)(const GqaParams, int, int), const
     if (device_sm_count(&sms) != 0) return B2D_ERR_CUDA;
     if (occupancy_per_sm(reinterpret_cast<const void*>(kern), threads, pl.smem, &per_sm))
       return B2D_ERR_CUDA;
-    per_sm = per_sm < 1 ? 1 : (per_sm > max_ctas_per_sm() ? max_ctas_per_sm() : per_sm);
+    const int cap = plan_ctas_per_sm(pl);
+    per_sm = per_sm < 1 ? 1 : (per_sm > cap ? cap : per_sm);
     ctas = sms * per_sm;
   }
   const int R = p.B * p.HG;
